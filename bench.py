@@ -1,0 +1,433 @@
+#!/usr/bin/env python
+"""bench.py -- K1 forward + backward throughput on B200, one process per GPU.
+
+Workload (the metric's single-GPU headline): bf16 logits
+[B=8, S=128, V=152064] ~ N(0, 3^2), targets sampled per row from softmax(logits),
+upstream gradients g_logp = -1/N, g_entropy = -0.01/N.  A step is one forward and one
+backward over that batch through the public API (kernel_opt.fused_logprob_entropy +
+torch.autograd.grad), inputs resident in HBM.  With --gpus N under torchrun every rank
+processes its own batch (row-sharded, weak scaling, no collective in the data path).
+
+Metric: algorithmic bytes per step / time, fwd = N V s + 20 N, bwd = 2 N V s + 28 N
+(s = 2 for bf16), reported in GB/s together with rows/s.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                  [--config c2|c3|c4-bf16|c4-fp16|c4-fp32] [--no-cpu-baseline]
+
+--impl reference times the reference's CPU path (TRL-1.4 selective_log_softmax +
+entropy_from_logits + autograd, restated in oracle/trl_eager.py since TRL is not
+installed) on the host cores, on rank 0 only.
+"""
+from __future__ import annotations
+
+import argparse
+import datetime
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+PKG_ROOT = os.path.join(REPO, "fused-logprob-entropy-cuda-kernel-for-llm-post-training_b200")
+for _p in (REPO, PKG_ROOT):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+import torch  # noqa: E402
+
+METRIC = "fwd+bwd HBM GB/s (% of B200 peak) and rows/s, V=152k bf16, 1/2/4/8 GPUs"
+UNIT = "GB/s"
+L2_BYTES = 126 * 1024 * 1024
+
+CONFIGS = {
+    "c2": dict(workload="baseline-config-2: single-GPU headline", B=8, S=128, V=152064,
+               dtype=torch.bfloat16, scale=3.0, window=False),
+    "c3": dict(workload="baseline-config-3: GRPO window logits[:, :-1] of [16,1025,V]", B=16,
+               S=1024, V=151936, dtype=torch.bfloat16, scale=2.5, window=True),
+    "c4-bf16": dict(workload="baseline-config-4: stress, bf16", B=1, S=8192, V=128256,
+                    dtype=torch.bfloat16, scale=2.0, window=False, spikes=True),
+    "c4-fp16": dict(workload="baseline-config-4: stress, fp16", B=1, S=8192, V=128256,
+                    dtype=torch.float16, scale=2.0, window=False, spikes=True),
+    "c4-fp32": dict(workload="baseline-config-4: stress, fp32", B=1, S=8192, V=128256,
+                    dtype=torch.float32, scale=2.0, window=False, spikes=True),
+}
+DTYPE_NAME = {torch.bfloat16: "bf16", torch.float16: "fp16", torch.float32: "fp32"}
+
+
+def algorithmic_bytes(n_rows: int, vocab: int, esize: int):
+    fwd = n_rows * vocab * esize + n_rows * (8 + 3 * 4)
+    bwd = 2 * n_rows * vocab * esize + n_rows * (8 + 2 * 4 + 3 * 4)
+    return fwd, bwd
+
+
+def measured_peak_gbs():
+    path = os.path.join(REPO, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+def committed_traffic(config_name: str):
+    """Per-launch DRAM bytes of the dominant kernel from the committed ncu summary."""
+    path = os.path.join(REPO, "profiles", "traffic.json")
+    try:
+        with open(path) as f:
+            return json.load(f).get(config_name)
+    except Exception:
+        return None
+
+
+# ---------------------------------------------------------------------------------------
+# Workload
+# ---------------------------------------------------------------------------------------
+def make_workload(cfg: dict, device, seed: int):
+    B, S, V, dt = cfg["B"], cfg["S"], cfg["V"], cfg["dtype"]
+    gen = torch.Generator(device=device).manual_seed(seed)
+    rows_total = B * (S + 1 if cfg["window"] else S)
+    parent = torch.empty((rows_total, V), dtype=dt, device=device)
+    chunk = 1024
+    for a in range(0, rows_total, chunk):
+        b = min(rows_total, a + chunk)
+        blk = torch.randn((b - a, V), generator=gen, device=device, dtype=torch.float32)
+        blk.mul_(cfg["scale"])
+        if cfg.get("spikes"):
+            spike = torch.rand((b - a, V), generator=gen, device=device) < 0.01
+            blk.add_(spike.float() * 15.0)
+            hot = torch.rand((b - a,), generator=gen, device=device) < 0.001
+            if hot.any():
+                col = torch.randint(0, V, (b - a,), generator=gen, device=device)
+                blk[hot, col[hot]] += 40.0
+        parent[a:b] = blk.to(dt)
+        del blk
+    if cfg["window"]:
+        logits = parent.view(B, S + 1, V)[:, :-1, :]
+    else:
+        logits = parent.view(B, S, V)
+    N = B * S
+    targets = torch.empty((B, S), dtype=torch.int64, device=device)
+    for bi in range(B):
+        for a in range(0, S, chunk):
+            b = min(S, a + chunk)
+            probs = torch.softmax(logits[bi, a:b].float(), dim=-1)
+            targets[bi, a:b] = torch.multinomial(probs, 1, generator=gen).view(-1)
+            del probs
+    g_lp = torch.full((B, S), -1.0 / N, device=device)
+    g_h = torch.full((B, S), -0.01 / N, device=device)
+    return logits, targets, g_lp, g_h
+
+
+# ---------------------------------------------------------------------------------------
+# Clock sampling (NVML, background thread, during the timed region)
+# ---------------------------------------------------------------------------------------
+class ClockSampler:
+    REASONS = {
+        "gpu_idle": 0x1, "applications_clocks_setting": 0x2, "sw_power_cap": 0x4,
+        "hw_slowdown": 0x8, "sync_boost": 0x10, "sw_thermal_slowdown": 0x20,
+        "hw_thermal_slowdown": 0x40, "hw_power_brake_slowdown": 0x80,
+    }
+
+    def __init__(self, device, period_s: float = 0.002):
+        self.samples, self.reasons, self.ok = [], 0, False
+        self.period = period_s
+        self._stop = threading.Event()
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self.nv = pynvml
+            props = torch.cuda.get_device_properties(device)
+            try:
+                bus = "%08x:%02x:%02x.0" % (props.pci_domain_id, props.pci_bus_id,
+                                            props.pci_device_id)
+                self.h = pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+            except Exception:
+                self.h = pynvml.nvmlDeviceGetHandleByIndex(device.index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+            self._reasons_fn = getattr(pynvml, "nvmlDeviceGetCurrentClocksEventReasons", None) \
+                or getattr(pynvml, "nvmlDeviceGetCurrentClocksThrottleReasons")
+            self.ok = True
+        except Exception:
+            self.max_mhz = None
+
+    def _run(self):
+        nv = self.nv
+        while not self._stop.is_set():
+            try:
+                self.samples.append(nv.nvmlDeviceGetClockInfo(self.h, nv.NVML_CLOCK_SM))
+                self.reasons |= self._reasons_fn(self.h)
+            except Exception:
+                pass
+            time.sleep(self.period)
+
+    def __enter__(self):
+        if self.ok:
+            self.t = threading.Thread(target=self._run, daemon=True)
+            self.t.start()
+        return self
+
+    def __exit__(self, *a):
+        if self.ok:
+            self._stop.set()
+            self.t.join()
+
+    def summary(self):
+        if not self.ok or not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": ["unavailable"],
+                    "samples": 0}
+        names = [k for k, bit in self.REASONS.items() if self.reasons & bit]
+        return {"sm_mhz": statistics.median(self.samples), "sm_max_mhz": self.max_mhz,
+                "reasons": names, "samples": len(self.samples)}
+
+
+# ---------------------------------------------------------------------------------------
+# CPU baseline: the reference's CPU path restated (oracle/trl_eager.py)
+# ---------------------------------------------------------------------------------------
+def cpu_trl_step_fn(logits_cpu, targets_cpu, g_lp_cpu, g_h_cpu):
+    from oracle import trl_eager
+
+    def step():
+        trl_eager.forward_backward(logits_cpu, targets_cpu, g_lp_cpu, g_h_cpu)
+    return step
+
+
+def time_cpu_baseline(logits, targets, g_lp, g_h, esize, budget_s=12.0):
+    x = logits.detach().cpu()
+    t, a, b = targets.cpu(), g_lp.cpu(), g_h.cpu()
+    step = cpu_trl_step_fn(x, t, a, b)
+    step()
+    t0 = time.perf_counter()
+    n = 0
+    while True:
+        step()
+        n += 1
+        if time.perf_counter() - t0 >= budget_s:
+            break
+    dt = (time.perf_counter() - t0) / n
+    N, V = t.numel(), x.shape[-1]
+    fwd, bwd = algorithmic_bytes(N, V, esize)
+    return {"value": round((fwd + bwd) / dt / 1e9, 4), "unit": UNIT,
+            "rows_per_s": round(N / dt, 2), "cores": torch.get_num_threads(), "kind": "port",
+            "sample": f"the full batch ({N} rows x {V}), {n} fwd+bwd steps in "
+                      f"{n * dt:.1f} s, TRL-1.4 eager path restated (oracle/trl_eager.py)"}
+
+
+# ---------------------------------------------------------------------------------------
+# Arms
+# ---------------------------------------------------------------------------------------
+def dist_env():
+    return (int(os.environ.get("RANK", "0")), int(os.environ.get("LOCAL_RANK", "0")),
+            int(os.environ.get("WORLD_SIZE", "1")))
+
+
+def reference_arm(args, cfg, rank, world):
+    if rank != 0:
+        return
+    from oracle import trl_eager
+    V, dt = cfg["V"], cfg["dtype"]
+    esize = torch.tensor([], dtype=dt).element_size()
+    B, S = cfg["B"], cfg["S"]
+    gen = torch.Generator().manual_seed(1234)
+    full = (torch.randn(B, S, V, generator=gen) * cfg["scale"]).to(dt)
+    targets = torch.randint(0, V, (B, S), generator=gen)
+    N = B * S
+    g_lp, g_h = torch.full((B, S), -1.0 / N), torch.full((B, S), -0.01 / N)
+    probe = time.perf_counter()
+    trl_eager.forward_backward(full, targets, g_lp, g_h)
+    probe = time.perf_counter() - probe
+    # Each step is the full batch unless the whole run would exceed ~3 minutes; then a
+    # leading block of batch elements is used.
+    budget = 180.0 / max(1, args.steps + args.warmup)
+    b_use = B if probe <= budget else max(1, int(B * budget / probe))
+    x, t = full[:b_use].contiguous(), targets[:b_use].contiguous()
+    gl, gh = g_lp[:b_use].contiguous(), g_h[:b_use].contiguous()
+    for _ in range(args.warmup):
+        trl_eager.forward_backward(x, t, gl, gh)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        trl_eager.forward_backward(x, t, gl, gh)
+    el = time.perf_counter() - t0
+    n_rows = b_use * S
+    fwd, bwd = algorithmic_bytes(n_rows, V, esize)
+    value = (fwd + bwd) * args.steps / el / 1e9
+    out = {
+        "metric": METRIC, "value": round(value, 4), "unit": UNIT, "impl": "reference",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(el / args.steps * 1e3, 3), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": DTYPE_NAME[dt], "data": "synthetic",
+        "rows_per_s": round(n_rows * args.steps / el, 2),
+        "config": {"workload": cfg["workload"], "global_batch": B, "seq_len": S, "vocab": V,
+                   "rows_per_step": n_rows, "parallelism": "cpu host threads"},
+        "cpu_baseline": {"value": round(value, 4), "unit": UNIT, "cores": torch.get_num_threads(),
+                         "kind": "port",
+                         "sample": f"{b_use}/{B} batch elements ({n_rows} rows x {V}) per step; "
+                                   "TRL-1.4 selective_log_softmax + entropy_from_logits + "
+                                   "autograd, restated in oracle/trl_eager.py"},
+        "e2e": {"value": round(value, 4), "unit": UNIT, "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(out), flush=True)
+
+
+def ours_arm(args, cfg, rank, local_rank, world):
+    import torch.distributed as dist
+
+    import kernel_opt
+
+    device = torch.device("cuda", local_rank)
+    torch.cuda.set_device(device)
+    if world > 1:
+        dist.init_process_group("nccl", rank=rank, world_size=world, device_id=device,
+                                timeout=datetime.timedelta(seconds=300))
+    V, dt = cfg["V"], cfg["dtype"]
+    esize = torch.tensor([], dtype=dt).element_size()
+    logits, targets, g_lp, g_h = make_workload(cfg, device, seed=1234 + rank)
+    N = targets.numel()
+    fwd_bytes, bwd_bytes = algorithmic_bytes(N, V, esize)
+    step_bytes = fwd_bytes + bwd_bytes
+    stream = torch.cuda.current_stream(device)
+
+    def step():
+        x = logits.detach().requires_grad_(True)
+        lp, h, _l = kernel_opt.fused_logprob_entropy(x, targets)
+        (d,) = torch.autograd.grad((lp, h), x, (g_lp, g_h))
+        return d
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local_rank])
+        torch.cuda.synchronize(device)
+
+    for _ in range(max(3, args.warmup)):
+        step()
+    barrier()
+
+    # ---- device-resident timing (value) --------------------------------------------
+    K = args.steps
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(K)]
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(device) as clocks:
+        barrier()
+        start.record(stream)
+        for i in range(K):
+            x = logits.detach().requires_grad_(True)
+            ev[i][0].record(stream)
+            lp, h, _l = kernel_opt.fused_logprob_entropy(x, targets)
+            ev[i][1].record(stream)
+            (d,) = torch.autograd.grad((lp, h), x, (g_lp, g_h))
+            ev[i][2].record(stream)
+            del d, lp, h, _l, x
+        stop.record(stream)
+        barrier()
+    total_ms = start.elapsed_time(stop)
+    fwd_ms = [e[0].elapsed_time(e[1]) for e in ev]
+    bwd_ms = [e[1].elapsed_time(e[2]) for e in ev]
+    t = torch.tensor([total_ms], device=device, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    max_ms = float(t.item())
+
+    # ---- end to end through the public API with host buffers (e2e) ----------------
+    pin = dict(pin_memory=True)
+    logits_h = torch.empty(logits.shape, dtype=dt, **pin)
+    logits_h.copy_(logits)
+    targets_h = targets.cpu().pin_memory()
+    glp_h, gh_h = g_lp.cpu().pin_memory(), g_h.cpu().pin_memory()
+    d_h = torch.empty(logits.shape, dtype=dt, **pin)
+    outs_h = [torch.empty(targets.shape, dtype=torch.float32, **pin) for _ in range(3)]
+    h2d = logits_h.numel() * esize + targets_h.numel() * 8 + 2 * glp_h.numel() * 4
+    d2h = d_h.numel() * esize + 3 * outs_h[0].numel() * 4
+
+    def e2e_step():
+        x = logits_h.to(device, non_blocking=True).requires_grad_(True)
+        tt = targets_h.to(device, non_blocking=True)
+        a, b = glp_h.to(device, non_blocking=True), gh_h.to(device, non_blocking=True)
+        lp, h, l = kernel_opt.fused_logprob_entropy(x, tt)
+        (d,) = torch.autograd.grad((lp, h), x, (a, b))
+        d_h.copy_(d, non_blocking=True)
+        for o, src in zip(outs_h, (lp, h, l)):
+            o.copy_(src.detach(), non_blocking=True)
+
+    for _ in range(2):
+        e2e_step()
+    barrier()
+    K2 = max(1, min(K, 20))
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(K2):
+        e2e_step()
+    e1.record(stream)
+    barrier()
+    e2e_ms = torch.tensor([e0.elapsed_time(e1)], device=device, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(e2e_ms, op=dist.ReduceOp.MAX)
+    e2e_ms = float(e2e_ms.item())
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = time_cpu_baseline(logits, targets, g_lp, g_h, esize)
+
+    if world > 1:
+        dist.barrier(device_ids=[local_rank])
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+
+    peak, peak_kind = measured_peak_gbs()
+    value = step_bytes * K * world / (max_ms / 1e3) / 1e9
+    bwd_avg = statistics.mean(bwd_ms)
+    fwd_avg = statistics.mean(fwd_ms)
+    achieved = bwd_bytes / (bwd_avg / 1e3) / 1e9
+    cfg_name = args.config
+    out = {
+        "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world, "steps": K,
+        "warmup": args.warmup, "ms_per_step": round(max_ms / K, 4), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": DTYPE_NAME[dt], "data": "synthetic",
+        "rows_per_s": round(N * K * world / (max_ms / 1e3), 1),
+        "pct_of_peak": round(100 * value / world / peak, 2),
+        "fwd": {"ms": round(fwd_avg, 5), "gbs": round(fwd_bytes / (fwd_avg / 1e3) / 1e9, 1)},
+        "bwd": {"ms": round(bwd_avg, 5), "gbs": round(achieved, 1)},
+        "config": {"workload": cfg["workload"], "global_batch": cfg["B"] * world,
+                   "seq_len": cfg["S"], "vocab": V, "rows_per_gpu": N,
+                   "parallelism": f"row-sharded x{world} (no collective)",
+                   "l2": (f"inputs larger than L2: {logits.numel() * esize / 2**20:.0f} MiB "
+                          f"logits read and written per step vs {L2_BYTES // 2**20} MiB L2")},
+        "roofline": {"bound": "hbm", "kernel": "k1_bwd_kernel", "achieved": round(achieved, 1),
+                     "peak": peak, "unit": "GB/s", "frac": round(achieved / peak, 4),
+                     "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs, copy)",
+                     "algorithmic_bytes_per_launch": bwd_bytes,
+                     "traffic": committed_traffic(cfg_name)},
+        "gpu_launches": 2 * K,
+        "e2e": {"value": round(step_bytes * K2 * world / (e2e_ms / 1e3) / 1e9, 3), "unit": UNIT,
+                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                "ms_per_step": round(e2e_ms / K2, 3), "steps": K2},
+        "clocks": clocks.summary(),
+    }
+    if cpu is not None:
+        out["cpu_baseline"] = cpu
+    print(json.dumps(out), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=100)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--config", choices=sorted(CONFIGS), default="c2")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    rank, local_rank, world = dist_env()
+    cfg = CONFIGS[args.config]
+    if args.impl == "reference":
+        reference_arm(args, cfg, rank, world)
+    else:
+        ours_arm(args, cfg, rank, local_rank, world)
+
+
+if __name__ == "__main__":
+    main()

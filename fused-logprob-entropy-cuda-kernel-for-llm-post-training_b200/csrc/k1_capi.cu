@@ -1,0 +1,433 @@
+// k1_capi.cu -- extern "C" entry points of libk1_b200.so (declared in
+// include/k1_logprob.h): argument validation, launch configuration, error reporting.
+//
+// The reference's host dispatch (csrc/fused_logprob.cu:284-458) validates torch
+// tensors with TORCH_CHECK and launches one 256-thread block per row.  Here the
+// validation is on raw pointers / sizes (the torch-facing checks live in the binding
+// layer, k1_torch_binding.cpp), and every kernel gets a grid of
+// (SM count) x (resident blocks per SM) blocks that split the flattened work evenly.
+#include <atomic>
+#include <cstdarg>
+#include <cstdio>
+#include <map>
+#include <mutex>
+#include <string>
+#include <utility>
+
+#include "k1_kernels.cuh"
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int code, const char* fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof buf, fmt, ap);
+    va_end(ap);
+    g_last_error = buf;
+    return code;
+}
+
+int check_launch(const char* what) {
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess)
+        return fail(K1_ERR_CUDA, "%s: kernel launch failed: %s", what, cudaGetErrorString(e));
+    return K1_OK;
+}
+
+constexpr int kThreads = 256;
+constexpr int kUnroll = 8;           // 16-byte vectors in flight per thread and chunk
+constexpr int kMaxDevices = 64;
+constexpr int kMaxBlocksPerSm = 8;   // grid cap used to size the workspace
+constexpr int64_t kMinUnitsPerBlockVec = (int64_t)kThreads * kUnroll;
+constexpr int64_t kMinUnitsPerBlockScalar = (int64_t)kThreads * 64;
+
+int elem_size(int dtype) { return dtype == K1_DTYPE_F32 ? 4 : 2; }
+
+int current_device(int* dev) {
+    cudaError_t e = cudaGetDevice(dev);
+    if (e != cudaSuccess) return fail(K1_ERR_CUDA, "cudaGetDevice: %s", cudaGetErrorString(e));
+    if (*dev < 0 || *dev >= kMaxDevices) return fail(K1_ERR_CUDA, "device ordinal %d out of range", *dev);
+    return K1_OK;
+}
+
+int sm_count(int dev, int* out) {
+    static std::atomic<int> cache[kMaxDevices];
+    int v = cache[dev].load(std::memory_order_relaxed);
+    if (v == 0) {
+        cudaError_t e = cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
+        if (e != cudaSuccess)
+            return fail(K1_ERR_CUDA, "cudaDeviceGetAttribute(SM count): %s", cudaGetErrorString(e));
+        cache[dev].store(v, std::memory_order_relaxed);
+    }
+    *out = v;
+    return K1_OK;
+}
+
+// Resident blocks per SM of one kernel instance, cached per (device, kernel).
+template <typename Kernel>
+int blocks_per_sm(Kernel kernel, int dev, int* out) {
+    static std::mutex mu;
+    static std::map<std::pair<int, const void*>, int> cache;
+    const auto key = std::make_pair(dev, reinterpret_cast<const void*>(kernel));
+    {
+        std::lock_guard<std::mutex> lock(mu);
+        auto it = cache.find(key);
+        if (it != cache.end()) {
+            *out = it->second;
+            return K1_OK;
+        }
+    }
+    int v = 0;
+    cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&v, kernel, kThreads, 0);
+    if (e != cudaSuccess) return fail(K1_ERR_CUDA, "occupancy query: %s", cudaGetErrorString(e));
+    if (v < 1) v = 1;
+    if (v > kMaxBlocksPerSm) v = kMaxBlocksPerSm;
+    std::lock_guard<std::mutex> lock(mu);
+    cache[key] = v;
+    *out = v;
+    return K1_OK;
+}
+
+struct Rows {
+    int64_t n_rows, vocab, inner_rows, inner_stride, outer_stride;
+};
+
+int check_rows(const char* fn, const Rows& L) {
+    if (L.n_rows < 0) return fail(K1_ERR_INVALID_ARGUMENT, "%s: n_rows must be >= 0", fn);
+    if (L.vocab < 1) return fail(K1_ERR_INVALID_ARGUMENT, "%s: vocab must be >= 1", fn);
+    if (L.inner_rows < 1 || L.n_rows % L.inner_rows != 0)
+        return fail(K1_ERR_INVALID_ARGUMENT,
+                    "%s: inner_rows (%lld) must be >= 1 and divide n_rows (%lld)", fn,
+                    (long long)L.inner_rows, (long long)L.n_rows);
+    if (L.inner_stride < 0 || L.outer_stride < 0)
+        return fail(K1_ERR_INVALID_ARGUMENT, "%s: strides must be >= 0", fn);
+    return K1_OK;
+}
+
+// Whether every row starts on a 16-byte boundary and holds whole 16-byte vectors.
+bool vector_ok(const void* base, int es, const Rows& L) {
+    if (reinterpret_cast<uintptr_t>(base) % 16 != 0) return false;
+    if ((L.vocab * es) % 16 != 0) return false;
+    if (L.inner_rows > 1 && (L.inner_stride * es) % 16 != 0) return false;
+    if (L.n_rows > L.inner_rows && (L.outer_stride * es) % 16 != 0) return false;
+    return true;
+}
+
+k1::RowLayout layout_of(const Rows& L) {
+    k1::RowLayout r;
+    r.inner_rows = L.inner_rows;
+    r.inner_stride = L.inner_stride;
+    r.outer_stride = L.outer_stride;
+    return r;
+}
+
+size_t workspace_bytes_for(int sms) {
+    const size_t g = (size_t)sms * kMaxBlocksPerSm;
+    return 2 * g * sizeof(k1::RowPartial) + g * sizeof(unsigned) + 64;
+}
+
+template <typename Kernel>
+int grid_for(Kernel kernel, int dev, int64_t total, int64_t min_units, int64_t* grid) {
+    int sms = 0, occ = 0;
+    int rc = sm_count(dev, &sms);
+    if (rc) return rc;
+    rc = blocks_per_sm(kernel, dev, &occ);
+    if (rc) return rc;
+    int64_t g = (int64_t)sms * occ;
+    int64_t need = (total + min_units - 1) / min_units;
+    if (need < 1) need = 1;
+    if (g > need) g = need;
+    if (g > total) g = total;
+    if (g < 1) g = 1;
+    *grid = g;
+    return K1_OK;
+}
+
+template <typename T, bool SHARD>
+int launch_forward(const char* fn, const void* logits, const Rows& L, int64_t col_offset,
+                   const int64_t* targets, float* logprob, float* entropy, float* lse,
+                   k1_partial* partials, void* workspace, size_t workspace_bytes,
+                   cudaStream_t stream) {
+    int dev = 0;
+    int rc = current_device(&dev);
+    if (rc) return rc;
+    int sms = 0;
+    rc = sm_count(dev, &sms);
+    if (rc) return rc;
+    if (workspace == nullptr || workspace_bytes < workspace_bytes_for(sms))
+        return fail(K1_ERR_WORKSPACE, "%s: workspace of %zu bytes required (got %zu)", fn,
+                    workspace_bytes_for(sms), workspace == nullptr ? (size_t)0 : workspace_bytes);
+    if (reinterpret_cast<uintptr_t>(workspace) % 16 != 0)
+        return fail(K1_ERR_INVALID_ARGUMENT, "%s: workspace must be 16-byte aligned", fn);
+
+    const int es = (int)sizeof(T);
+    const bool vec = vector_ok(logits, es, L);
+    k1::FwdParams p;
+    p.logits = logits;
+    p.n_rows = L.n_rows;
+    p.vocab = L.vocab;
+    p.lay = layout_of(L);
+    p.vpr = vec ? L.vocab / k1::DT<T>::kEPV : L.vocab;
+    p.total = L.n_rows * p.vpr;
+    p.col_offset = col_offset;
+    p.targets = targets;
+    p.logprob = logprob;
+    p.entropy = entropy;
+    p.lse = lse;
+    p.partials = partials;
+    const size_t gmax = (size_t)sms * kMaxBlocksPerSm;
+    p.ws_part = reinterpret_cast<k1::RowPartial*>(workspace);
+    p.ws_ticket = reinterpret_cast<unsigned*>(reinterpret_cast<char*>(workspace) +
+                                              2 * gmax * sizeof(k1::RowPartial));
+    int64_t grid = 1;
+    if (vec) {
+        auto kern = k1::k1_fwd_kernel<T, kThreads, kUnroll, true, SHARD>;
+        rc = grid_for(kern, dev, p.total, kMinUnitsPerBlockVec, &grid);
+        if (rc) return rc;
+        kern<<<(unsigned)grid, kThreads, 0, stream>>>(p);
+    } else {
+        auto kern = k1::k1_fwd_kernel<T, kThreads, kUnroll, false, SHARD>;
+        rc = grid_for(kern, dev, p.total, kMinUnitsPerBlockScalar, &grid);
+        if (rc) return rc;
+        kern<<<(unsigned)grid, kThreads, 0, stream>>>(p);
+    }
+    return check_launch(fn);
+}
+
+template <typename T>
+int launch_backward(const char* fn, const void* logits, const Rows& L, const Rows& D,
+                    int64_t col_offset, const int64_t* targets, const float* lse,
+                    const float* entropy, const float* g_logp, const float* g_ent,
+                    const float* g_lse, void* d_logits, cudaStream_t stream) {
+    int dev = 0;
+    int rc = current_device(&dev);
+    if (rc) return rc;
+    const int es = (int)sizeof(T);
+    const bool vec = vector_ok(logits, es, L) && vector_ok(d_logits, es, D);
+    k1::BwdParams p;
+    p.logits = logits;
+    p.dlogits = d_logits;
+    p.n_rows = L.n_rows;
+    p.vocab = L.vocab;
+    p.lay = layout_of(L);
+    p.dlay = layout_of(D);
+    p.vpr = vec ? L.vocab / k1::DT<T>::kEPV : L.vocab;
+    p.total = L.n_rows * p.vpr;
+    p.col_offset = col_offset;
+    p.targets = targets;
+    p.lse = lse;
+    p.entropy = entropy;
+    p.g_logp = g_logp;
+    p.g_ent = g_ent;
+    p.g_lse = g_lse;
+    int64_t grid = 1;
+    if (vec) {
+        auto kern = k1::k1_bwd_kernel<T, kThreads, kUnroll, true>;
+        rc = grid_for(kern, dev, p.total, kMinUnitsPerBlockVec, &grid);
+        if (rc) return rc;
+        kern<<<(unsigned)grid, kThreads, 0, stream>>>(p);
+    } else {
+        auto kern = k1::k1_bwd_kernel<T, kThreads, kUnroll, false>;
+        rc = grid_for(kern, dev, p.total, kMinUnitsPerBlockScalar, &grid);
+        if (rc) return rc;
+        kern<<<(unsigned)grid, kThreads, 0, stream>>>(p);
+    }
+    return check_launch(fn);
+}
+
+int check_common(const char* fn, const void* logits, int dtype, const Rows& L) {
+    if (dtype != K1_DTYPE_F32 && dtype != K1_DTYPE_F16 && dtype != K1_DTYPE_BF16)
+        return fail(K1_ERR_UNSUPPORTED_DTYPE, "%s: logits dtype must be bf16, fp16, or fp32", fn);
+    int rc = check_rows(fn, L);
+    if (rc) return rc;
+    if (L.n_rows > 0 && logits == nullptr)
+        return fail(K1_ERR_INVALID_ARGUMENT, "%s: logits is NULL", fn);
+    if (reinterpret_cast<uintptr_t>(logits) % elem_size(dtype) != 0)
+        return fail(K1_ERR_INVALID_ARGUMENT, "%s: logits not aligned to its element size", fn);
+    return K1_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* k1_last_error(void) { return g_last_error.c_str(); }
+
+int k1_abi_version(void) { return K1_ABI_VERSION; }
+
+size_t k1_forward_workspace_bytes(int64_t n_rows, int64_t vocab, int dtype, int device) {
+    (void)n_rows;
+    (void)vocab;
+    (void)dtype;
+    if (device < 0 || device >= kMaxDevices) return 0;
+    int sms = 0;
+    if (sm_count(device, &sms) != K1_OK) return 0;
+    return workspace_bytes_for(sms);
+}
+
+int k1_fused_logprob_entropy_v1(const void* logits, int dtype, int64_t n_rows, int64_t vocab,
+                                int64_t inner_rows, int64_t inner_stride, int64_t outer_stride,
+                                const int64_t* targets, float* logprob, float* entropy,
+                                float* lse, void* workspace, size_t workspace_bytes,
+                                void* stream) {
+    static const char* fn = "k1_fused_logprob_entropy_v1";
+    Rows L{n_rows, vocab, inner_rows, inner_stride, outer_stride};
+    int rc = check_common(fn, logits, dtype, L);
+    if (rc) return rc;
+    if (n_rows == 0) return K1_OK;
+    if (!targets || !logprob || !entropy || !lse)
+        return fail(K1_ERR_INVALID_ARGUMENT, "%s: NULL targets or output pointer", fn);
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    switch (dtype) {
+        case K1_DTYPE_BF16:
+            return launch_forward<__nv_bfloat16, false>(fn, logits, L, 0, targets, logprob, entropy,
+                                                        lse, nullptr, workspace, workspace_bytes, s);
+        case K1_DTYPE_F16:
+            return launch_forward<__half, false>(fn, logits, L, 0, targets, logprob, entropy, lse,
+                                                 nullptr, workspace, workspace_bytes, s);
+        default:
+            return launch_forward<float, false>(fn, logits, L, 0, targets, logprob, entropy, lse,
+                                                nullptr, workspace, workspace_bytes, s);
+    }
+}
+
+int k1_fused_logprob_entropy_naive(const void* logits, int dtype, int64_t n_rows, int64_t vocab,
+                                   int64_t inner_rows, int64_t inner_stride,
+                                   int64_t outer_stride, const int64_t* targets,
+                                   float* logprob, float* entropy, float* lse, void* stream) {
+    static const char* fn = "k1_fused_logprob_entropy_naive";
+    Rows L{n_rows, vocab, inner_rows, inner_stride, outer_stride};
+    int rc = check_common(fn, logits, dtype, L);
+    if (rc) return rc;
+    if (n_rows == 0) return K1_OK;
+    if (!targets || !logprob || !entropy || !lse)
+        return fail(K1_ERR_INVALID_ARGUMENT, "%s: NULL targets or output pointer", fn);
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    const int threads = 128;
+    const int64_t blocks = (n_rows + threads - 1) / threads;
+    k1::RowLayout lay = layout_of(L);
+    switch (dtype) {
+        case K1_DTYPE_BF16:
+            k1::k1_naive_kernel<__nv_bfloat16><<<(unsigned)blocks, threads, 0, s>>>(
+                reinterpret_cast<const __nv_bfloat16*>(logits), n_rows, vocab, lay, targets,
+                logprob, entropy, lse);
+            break;
+        case K1_DTYPE_F16:
+            k1::k1_naive_kernel<__half><<<(unsigned)blocks, threads, 0, s>>>(
+                reinterpret_cast<const __half*>(logits), n_rows, vocab, lay, targets, logprob,
+                entropy, lse);
+            break;
+        default:
+            k1::k1_naive_kernel<float><<<(unsigned)blocks, threads, 0, s>>>(
+                reinterpret_cast<const float*>(logits), n_rows, vocab, lay, targets, logprob,
+                entropy, lse);
+            break;
+    }
+    return check_launch(fn);
+}
+
+static int backward_impl(const char* fn, const void* logits, int dtype, int64_t n_rows,
+                         int64_t vocab, int64_t inner_rows, int64_t inner_stride,
+                         int64_t outer_stride, int64_t col_offset, const int64_t* targets,
+                         const float* lse, const float* entropy, const float* g_logp,
+                         const float* g_ent, const float* g_lse, void* d_logits,
+                         int64_t d_inner_stride, int64_t d_outer_stride, void* stream) {
+    Rows L{n_rows, vocab, inner_rows, inner_stride, outer_stride};
+    Rows D{n_rows, vocab, inner_rows, d_inner_stride, d_outer_stride};
+    int rc = check_common(fn, logits, dtype, L);
+    if (rc) return rc;
+    rc = check_rows(fn, D);
+    if (rc) return rc;
+    if (n_rows == 0) return K1_OK;
+    if (!targets || !lse || !entropy || !d_logits)
+        return fail(K1_ERR_INVALID_ARGUMENT, "%s: NULL targets, lse, entropy or d_logits", fn);
+    if (reinterpret_cast<uintptr_t>(d_logits) % elem_size(dtype) != 0)
+        return fail(K1_ERR_INVALID_ARGUMENT, "%s: d_logits not aligned to its element size", fn);
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    switch (dtype) {
+        case K1_DTYPE_BF16:
+            return launch_backward<__nv_bfloat16>(fn, logits, L, D, col_offset, targets, lse,
+                                                  entropy, g_logp, g_ent, g_lse, d_logits, s);
+        case K1_DTYPE_F16:
+            return launch_backward<__half>(fn, logits, L, D, col_offset, targets, lse, entropy,
+                                           g_logp, g_ent, g_lse, d_logits, s);
+        default:
+            return launch_backward<float>(fn, logits, L, D, col_offset, targets, lse, entropy,
+                                          g_logp, g_ent, g_lse, d_logits, s);
+    }
+}
+
+int k1_fused_logprob_entropy_v1_backward(
+    const void* logits, int dtype, int64_t n_rows, int64_t vocab, int64_t inner_rows,
+    int64_t inner_stride, int64_t outer_stride, const int64_t* targets, const float* lse,
+    const float* entropy, const float* g_logp, const float* g_ent, const float* g_lse,
+    void* d_logits, int64_t d_inner_stride, int64_t d_outer_stride, void* stream) {
+    return backward_impl("k1_fused_logprob_entropy_v1_backward", logits, dtype, n_rows, vocab,
+                         inner_rows, inner_stride, outer_stride, 0, targets, lse, entropy,
+                         g_logp, g_ent, g_lse, d_logits, d_inner_stride, d_outer_stride, stream);
+}
+
+int k1_vocab_shard_partials(const void* logits, int dtype, int64_t n_rows, int64_t shard_vocab,
+                            int64_t inner_rows, int64_t inner_stride, int64_t outer_stride,
+                            int64_t vocab_offset, const int64_t* targets,
+                            k1_partial* partials, void* workspace, size_t workspace_bytes,
+                            void* stream) {
+    static const char* fn = "k1_vocab_shard_partials";
+    Rows L{n_rows, shard_vocab, inner_rows, inner_stride, outer_stride};
+    int rc = check_common(fn, logits, dtype, L);
+    if (rc) return rc;
+    if (vocab_offset < 0) return fail(K1_ERR_INVALID_ARGUMENT, "%s: vocab_offset must be >= 0", fn);
+    if (n_rows == 0) return K1_OK;
+    if (!targets || !partials)
+        return fail(K1_ERR_INVALID_ARGUMENT, "%s: NULL targets or partials", fn);
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    switch (dtype) {
+        case K1_DTYPE_BF16:
+            return launch_forward<__nv_bfloat16, true>(fn, logits, L, vocab_offset, targets,
+                                                       nullptr, nullptr, nullptr, partials,
+                                                       workspace, workspace_bytes, s);
+        case K1_DTYPE_F16:
+            return launch_forward<__half, true>(fn, logits, L, vocab_offset, targets, nullptr,
+                                                nullptr, nullptr, partials, workspace,
+                                                workspace_bytes, s);
+        default:
+            return launch_forward<float, true>(fn, logits, L, vocab_offset, targets, nullptr,
+                                               nullptr, nullptr, partials, workspace,
+                                               workspace_bytes, s);
+    }
+}
+
+int k1_vocab_combine(const k1_partial* gathered, int n_shards, int64_t n_rows, float* logprob,
+                     float* entropy, float* lse, void* stream) {
+    static const char* fn = "k1_vocab_combine";
+    if (n_shards < 1) return fail(K1_ERR_INVALID_ARGUMENT, "%s: n_shards must be >= 1", fn);
+    if (n_rows < 0) return fail(K1_ERR_INVALID_ARGUMENT, "%s: n_rows must be >= 0", fn);
+    if (n_rows == 0) return K1_OK;
+    if (!gathered || !logprob || !entropy || !lse)
+        return fail(K1_ERR_INVALID_ARGUMENT, "%s: NULL pointer argument", fn);
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    const int threads = 128;
+    const int64_t blocks = (n_rows + threads - 1) / threads;
+    k1::k1_vocab_combine_kernel<<<(unsigned)blocks, threads, 0, s>>>(gathered, n_shards, n_rows,
+                                                                     logprob, entropy, lse);
+    return check_launch(fn);
+}
+
+int k1_vocab_shard_backward(const void* logits, int dtype, int64_t n_rows, int64_t shard_vocab,
+                            int64_t inner_rows, int64_t inner_stride, int64_t outer_stride,
+                            int64_t vocab_offset, const int64_t* targets, const float* lse,
+                            const float* entropy, const float* g_logp, const float* g_ent,
+                            const float* g_lse, void* d_logits, int64_t d_inner_stride,
+                            int64_t d_outer_stride, void* stream) {
+    if (vocab_offset < 0)
+        return fail(K1_ERR_INVALID_ARGUMENT, "k1_vocab_shard_backward: vocab_offset must be >= 0");
+    return backward_impl("k1_vocab_shard_backward", logits, dtype, n_rows, shard_vocab,
+                         inner_rows, inner_stride, outer_stride, vocab_offset, targets, lse,
+                         entropy, g_logp, g_ent, g_lse, d_logits, d_inner_stride,
+                         d_outer_stride, stream);
+}
+
+}  // extern "C"

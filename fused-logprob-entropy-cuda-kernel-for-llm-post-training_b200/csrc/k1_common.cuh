@@ -1,0 +1,333 @@
+// k1_common.cuh -- device building blocks shared by the K1 kernels (sm_100a).
+//
+// Streaming state.  The reference keeps one (m, Z, T) triple per thread and merges a
+// one-element state into it for every logit, which costs two exponentials per element
+// (csrc/fused_logprob.cu:141-154, 183-188).  Here a thread loads a chunk of logits,
+// folds the chunk maximum with packed bf16x2 / f16x2 max instructions, rescales its
+// state once per chunk, and then spends exactly one ex2 per element.  Arithmetic uses
+// the Blackwell packed f32x2 add / mul / fma, two logits per instruction.
+//
+// Precision.  Z = sum exp(x - m) is kept as two fp32 pairs: `zb` holds each term
+// rounded to a multiple of 2^-10 (exact while the sum stays below 2^14) and `zs` the
+// remainder.  For a near-one-hot row (one logit far above the rest) the maximum's term
+// is exactly 1 and lands in zb, while every tail term lands in zs with full relative
+// precision; a single fp32 accumulator would round the tail away and lose the
+// entropy.  T = sum exp(x - m)(x - m) is a sum of non-positive terms, so it never
+// cancels.  Thread and block states are merged in fp64.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace k1 {
+
+constexpr float kLog2e = 1.4426950408889634f;
+// (e + kSplit) - kSplit rounds e in [0, 1] to a multiple of 2^-10.
+constexpr float kSplit = 8192.0f;
+// fp32 logits are clamped to this before use, so x - m stays finite for x = -inf.
+constexpr float kClampF32 = -1.0e38f;
+
+// ---------------------------------------------------------------------------------
+// Scalar / packed primitives
+// ---------------------------------------------------------------------------------
+__device__ __forceinline__ float ex2(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+// NaN-propagating max (fmaxf drops NaN; the reference's outputs become NaN when a
+// row holds one, and so do ours).
+__device__ __forceinline__ float fmax_nan(float a, float b) {
+    float y;
+    asm("max.NaN.f32 %0, %1, %2;" : "=f"(y) : "f"(a), "f"(b));
+    return y;
+}
+
+__device__ __forceinline__ float2 add2(float2 a, float2 b) { return __fadd2_rn(a, b); }
+__device__ __forceinline__ float2 mul2(float2 a, float2 b) { return __fmul2_rn(a, b); }
+__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) { return __ffma2_rn(a, b, c); }
+__device__ __forceinline__ float2 sub2(float2 a, float2 b) {
+    uint64_t ra, rb, rd;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(ra) : "f"(a.x), "f"(a.y));
+    asm("mov.b64 %0, {%1, %2};" : "=l"(rb) : "f"(b.x), "f"(b.y));
+    asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(rd) : "l"(ra), "l"(rb));
+    float2 d;
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(d.x), "=f"(d.y) : "l"(rd));
+    return d;
+}
+__device__ __forceinline__ float2 splat(float v) { return make_float2(v, v); }
+
+// Streaming 16-byte load: read once, do not keep in L1.
+__device__ __forceinline__ uint4 ldg_stream(const void* p) {
+    uint4 v;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "l"(p));
+    return v;
+}
+
+__device__ __forceinline__ void stg_stream(void* p, uint4 v) {
+    asm volatile("st.global.v4.u32 [%0], {%1, %2, %3, %4};" ::"l"(p), "r"(v.x), "r"(v.y),
+                 "r"(v.z), "r"(v.w)
+                 : "memory");
+}
+
+// ---------------------------------------------------------------------------------
+// Element types.  A 16-byte vector holds kEPV elements; for the 16-bit types it is
+// four 32-bit words of two elements each.
+// ---------------------------------------------------------------------------------
+template <typename T>
+struct DT;
+
+template <>
+struct DT<__nv_bfloat16> {
+    static constexpr int kEPV = 8;
+    static constexpr uint32_t kLowest2 = 0xFF7FFF7Fu;  // lowest finite bf16, both halves
+    static constexpr float kLowest = -3.38953138925153547590470800371487866880e38f;
+    __device__ static __forceinline__ uint32_t clamp2(uint32_t w) {
+        uint32_t r;
+        asm("max.NaN.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(w), "r"(kLowest2));
+        return r;
+    }
+    __device__ static __forceinline__ uint32_t max2(uint32_t a, uint32_t b) {
+        uint32_t r;
+        asm("max.NaN.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+        return r;
+    }
+    __device__ static __forceinline__ float2 to_f2(uint32_t w) {
+        return make_float2(__uint_as_float(w << 16), __uint_as_float(w & 0xffff0000u));
+    }
+    __device__ static __forceinline__ uint32_t from_f2(float2 v) {
+        uint32_t r;
+        asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(v.y), "f"(v.x));
+        return r;
+    }
+    __device__ static __forceinline__ float load1(const __nv_bfloat16* p) {
+        return __bfloat162float(*p);
+    }
+    __device__ static __forceinline__ void store1(__nv_bfloat16* p, float v) {
+        *p = __float2bfloat16_rn(v);
+    }
+    __device__ static __forceinline__ float clamp1(float x) { return fmax_nan(x, kLowest); }
+};
+
+template <>
+struct DT<__half> {
+    static constexpr int kEPV = 8;
+    static constexpr uint32_t kLowest2 = 0xFBFFFBFFu;  // -65504, both halves
+    static constexpr float kLowest = -65504.0f;
+    __device__ static __forceinline__ uint32_t clamp2(uint32_t w) {
+        uint32_t r;
+        asm("max.NaN.f16x2 %0, %1, %2;" : "=r"(r) : "r"(w), "r"(kLowest2));
+        return r;
+    }
+    __device__ static __forceinline__ uint32_t max2(uint32_t a, uint32_t b) {
+        uint32_t r;
+        asm("max.NaN.f16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+        return r;
+    }
+    __device__ static __forceinline__ float2 to_f2(uint32_t w) {
+        __half2 h = *reinterpret_cast<__half2*>(&w);
+        return __half22float2(h);
+    }
+    __device__ static __forceinline__ uint32_t from_f2(float2 v) {
+        uint32_t r;
+        asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(v.y), "f"(v.x));
+        return r;
+    }
+    __device__ static __forceinline__ float load1(const __half* p) { return __half2float(*p); }
+    __device__ static __forceinline__ void store1(__half* p, float v) { *p = __float2half_rn(v); }
+    __device__ static __forceinline__ float clamp1(float x) { return fmax_nan(x, kLowest); }
+};
+
+template <>
+struct DT<float> {
+    static constexpr int kEPV = 4;
+    static constexpr float kLowest = kClampF32;
+    __device__ static __forceinline__ float load1(const float* p) { return *p; }
+    __device__ static __forceinline__ void store1(float* p, float v) { *p = v; }
+    __device__ static __forceinline__ float clamp1(float x) { return fmax_nan(x, kClampF32); }
+};
+
+// ---------------------------------------------------------------------------------
+// Forward streaming state of one thread (see the header comment).
+// ---------------------------------------------------------------------------------
+struct FwdState {
+    float m;     // running maximum (clamped logits); <= kLowest of the type means "empty"
+    float2 zb;   // sum of exp(x - m) rounded to multiples of 2^-10
+    float2 zs;   // remainders
+    float2 t;    // sum of exp(x - m) * (x - m)
+
+    __device__ __forceinline__ void init() {
+        m = -3.402823466e38f;
+        zb = splat(0.f);
+        zs = splat(0.f);
+        t = splat(0.f);
+    }
+
+    // Move the reference point to max(m, mc).  Exact no-op when the maximum is unchanged.
+    __device__ __forceinline__ void rescale(float mc) {
+        float mn = fmax_nan(m, mc);
+        float dl = m - mn;  // <= 0, or NaN
+        float s = (dl == 0.f) ? 1.f : ex2(dl * kLog2e);
+        float2 s2 = splat(s);
+        float2 z = add2(zb, zs);
+        t = mul2(fma2(splat(dl), z, t), s2);
+        zb = mul2(zb, s2);
+        zs = mul2(zs, s2);
+        float2 g = sub2(add2(zb, splat(kSplit)), splat(kSplit));
+        zs = add2(zs, sub2(zb, g));
+        zb = g;
+        m = mn;
+    }
+
+    // Accumulate two clamped logits; nm = (-m, -m).
+    __device__ __forceinline__ void accum(float2 x, float2 nm) {
+        float2 d = add2(x, nm);
+        float2 tt = mul2(d, splat(kLog2e));
+        float2 e = make_float2(ex2(tt.x), ex2(tt.y));
+        float2 g = sub2(add2(e, splat(kSplit)), splat(kSplit));
+        zb = add2(zb, g);
+        zs = add2(zs, sub2(e, g));
+        t = fma2(e, d, t);
+    }
+};
+
+// Row (or row-segment) state after a block reduction, relative to its maximum m.
+// m = -inf with z = t = 0 is the empty state (every logit -inf); NaN m poisons.
+struct RowPartial {
+    double z;
+    double t;
+    float m;
+    float pad;
+};
+
+// ---------------------------------------------------------------------------------
+// Reductions
+// ---------------------------------------------------------------------------------
+__device__ __forceinline__ float warp_max_nan(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmax_nan(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
+__device__ __forceinline__ double warp_sum(double v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+// Shared scratch for one block reduction.
+template <int THREADS>
+struct ReduceSmem {
+    float wmax[THREADS / 32];
+    double wz[THREADS / 32];
+    double wt[THREADS / 32];
+};
+
+// Merge every thread's (m, z, t) -- z, t relative to that thread's own m -- into the
+// block's state relative to the block maximum.  `empty` threads contribute nothing.
+// The result is valid in every thread.  Contains __syncthreads(): call uniformly.
+template <int THREADS>
+__device__ __forceinline__ RowPartial block_merge(float m, double z, double t, bool empty,
+                                                  ReduceSmem<THREADS>& sm) {
+    constexpr int NW = THREADS / 32;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    float mm = empty ? -INFINITY : m;
+    float wm = warp_max_nan(mm);
+    if (lane == 0) sm.wmax[warp] = wm;
+    __syncthreads();
+    float M = sm.wmax[0];
+#pragma unroll
+    for (int i = 1; i < NW; ++i) M = fmax_nan(M, sm.wmax[i]);
+    double zc = 0.0, tc = 0.0;
+    if (!empty) {
+        float dm = m - M;  // <= 0, NaN if M or m is NaN
+        float s = (dm == 0.f) ? 1.f : ex2(dm * kLog2e);
+        zc = (double)s * z;
+        tc = (double)s * (t + (double)dm * z);
+    }
+    zc = warp_sum(zc);
+    tc = warp_sum(tc);
+    if (lane == 0) {
+        sm.wz[warp] = zc;
+        sm.wt[warp] = tc;
+    }
+    __syncthreads();
+    RowPartial r;
+    r.z = 0.0;
+    r.t = 0.0;
+#pragma unroll
+    for (int i = 0; i < NW; ++i) {
+        r.z += sm.wz[i];
+        r.t += sm.wt[i];
+    }
+    r.m = M;  // NaN poisons; -inf means every thread was empty
+    if (M == -INFINITY) {
+        r.z = 0.0;
+        r.t = 0.0;
+    }
+    r.pad = 0.f;
+    __syncthreads();  // smem is reused by the caller's next reduction
+    return r;
+}
+
+// Merge two row partials (associative; fp64).  The reference's combine rule
+// (csrc/fused_logprob.cu:119-154) with the -inf sentinel, evaluated in fp64.
+__device__ __forceinline__ RowPartial merge_partials(RowPartial a, RowPartial b) {
+    if (isnan(a.m) || isnan(b.m)) {
+        RowPartial r = a;
+        r.m = __int_as_float(0x7fc00000);
+        return r;
+    }
+    if (b.m == -INFINITY) return a;
+    if (a.m == -INFINITY) return b;
+    float M = fmaxf(a.m, b.m);
+    double da = (double)a.m - (double)M, db = (double)b.m - (double)M;
+    double sa = exp(da), sb = exp(db);
+    RowPartial r;
+    r.m = M;
+    r.z = sa * a.z + sb * b.z;
+    r.t = sa * (a.t + da * a.z) + sb * (b.t + db * b.z);
+    r.pad = 0.f;
+    return r;
+}
+
+// Final per-row values from a merged partial and the target logit.
+__device__ __forceinline__ void finalize_row(RowPartial p, double x_t, float* logprob,
+                                             float* entropy, float* lse) {
+    double l, h, lp;
+    if (isnan(p.m)) {
+        l = h = lp = (double)__int_as_float(0x7fc00000);
+    } else if (p.m == -INFINITY) {
+        l = -INFINITY;
+        h = (double)__int_as_float(0x7fc00000);
+        lp = x_t - l;
+    } else {
+        double logz = log(p.z);
+        l = (double)p.m + logz;
+        h = logz - p.t / p.z;
+        lp = x_t - l;
+    }
+    *logprob = (float)lp;
+    *entropy = (float)h;
+    *lse = (float)l;
+}
+
+// ---------------------------------------------------------------------------------
+// Row addressing (two stride levels, see include/k1_logprob.h)
+// ---------------------------------------------------------------------------------
+struct RowLayout {
+    int64_t inner_rows;
+    int64_t inner_stride;
+    int64_t outer_stride;
+    __device__ __forceinline__ int64_t offset(int64_t r) const {
+        int64_t o = r / inner_rows;
+        return o * outer_stride + (r - o * inner_rows) * inner_stride;
+    }
+};
+
+}  // namespace k1

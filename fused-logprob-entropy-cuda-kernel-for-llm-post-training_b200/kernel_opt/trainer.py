@@ -1,0 +1,76 @@
+"""KernelOptGRPOTrainer -- trl.GRPOTrainer with the logprob/entropy block replaced by K1.
+
+Same override as the reference (python/kernel_opt/trainer.py:1-131): only
+`_get_per_token_logps_and_entropies` changes, which is TRL's single entry point for the
+policy, old-policy and reference log-prob computations.  Multimodal inputs fall back to
+the parent.  Unlike the reference, the completion window of each chunk is one K1 launch
+on the strided [B, L', V] view instead of a loop over batch elements.
+
+Requires `trl` (imported at module load, as in the reference); `kernel_opt` imports
+this module lazily.
+"""
+from __future__ import annotations
+
+import torch
+from trl import GRPOTrainer
+
+from .grpo import MULTIMODAL_KWARGS, completion_window, k1_logps_and_entropies
+
+
+class KernelOptGRPOTrainer(GRPOTrainer):
+    """trl.GRPOTrainer with the inner logprob+entropy block replaced by K1."""
+
+    def _get_per_token_logps_and_entropies(
+        self,
+        model,
+        input_ids,
+        attention_mask,
+        logits_to_keep,
+        batch_size=None,
+        compute_entropy=False,
+        pixel_values=None,
+        image_grid_thw=None,
+        num_images=None,
+        pixel_attention_mask=None,
+        image_sizes=None,
+        token_type_ids=None,
+        mm_token_type_ids=None,
+        image_position_ids=None,
+    ) -> tuple[torch.Tensor, torch.Tensor | None]:
+        extra = dict(
+            pixel_values=pixel_values, image_grid_thw=image_grid_thw, num_images=num_images,
+            pixel_attention_mask=pixel_attention_mask, image_sizes=image_sizes,
+            token_type_ids=token_type_ids, mm_token_type_ids=mm_token_type_ids,
+            image_position_ids=image_position_ids,
+        )
+        assert set(extra) == set(MULTIMODAL_KWARGS)
+        if any(v is not None for v in extra.values()):
+            return super()._get_per_token_logps_and_entropies(
+                model, input_ids, attention_mask, logits_to_keep,
+                batch_size=batch_size, compute_entropy=compute_entropy, **extra)
+
+        bsz = batch_size or input_ids.size(0)
+        all_logps: list[torch.Tensor] = []
+        all_entropies: list[torch.Tensor] = []
+        for start in range(0, input_ids.size(0), bsz):
+            input_ids_batch = input_ids[start:start + bsz]
+            attention_mask_batch = attention_mask[start:start + bsz]
+            model_inputs = {"input_ids": input_ids_batch,
+                            "attention_mask": attention_mask_batch}
+            if "logits_to_keep" in self.model_kwarg_keys:
+                # +1 because the last position is dropped below
+                model_inputs["logits_to_keep"] = logits_to_keep + 1
+            model_inputs["use_cache"] = False
+
+            logits = model(**model_inputs).logits
+            logits = completion_window(logits, logits_to_keep)
+            logits.div_(self.temperature)  # in place, as TRL does
+            completion_ids = input_ids_batch[:, -logits_to_keep:]
+            logps, ents = k1_logps_and_entropies(logits, completion_ids, compute_entropy)
+            all_logps.append(logps)
+            if compute_entropy:
+                all_entropies.append(ents)
+
+        logps = torch.cat(all_logps, dim=0)
+        entropies = torch.cat(all_entropies, dim=0) if compute_entropy else None
+        return logps, entropies

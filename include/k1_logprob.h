@@ -1,0 +1,168 @@
+/*
+ * k1_logprob.h -- C ABI of the B200 (sm_100a) K1 primitive: per-row log-prob of a
+ * target token, entropy and log-sum-exp over a [rows, vocab] block of logits,
+ * forward and backward.
+ *
+ * Every entry point takes plain device pointers, element counts/strides and a CUDA
+ * stream handle (cudaStream_t passed as void*; NULL = legacy default stream).  No
+ * entry point allocates device memory, synchronises the stream, or keeps state
+ * between calls other than a cached per-device SM count.  The caller owns every
+ * output buffer, exactly like the reference's torch binding, whose host functions
+ * only write into out-parameters (reference: csrc/fused_logprob.cu:284-458,
+ * python/kernel_opt/ops.py:24-30,83).
+ *
+ * Row layout.  Rows are addressed with two stride levels so that a sliced
+ * [B, L', V] view such as logits[:, :-1, :] of a [B, L, V] tensor is one call:
+ *     element (r, v) lives at  base + (r / inner_rows) * outer_stride
+ *                                   + (r % inner_rows) * inner_stride + v
+ * A contiguous [N, V] matrix is inner_rows = N, inner_stride = V (outer_stride is
+ * then unused).  The vocabulary axis always has unit stride.  The reference only
+ * accepts contiguous logits (csrc/fused_logprob.cu:294,364,414).
+ *
+ * Targets outside [0, vocab) (for example an ignore index of -100) are accepted
+ * and follow the reference kernels: the target logit reads as 0, so
+ * logprob = -lse, and the backward adds no one-hot term
+ * (csrc/fused_logprob.cu:179-185, 279).
+ *
+ * Return value: K1_OK (0) or a k1_status code; k1_last_error() then returns a
+ * message for the calling thread.  Kernel launch errors are reported the same way
+ * (the reference does not check launches).
+ */
+#ifndef K1_LOGPROB_H
+#define K1_LOGPROB_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define K1_ABI_VERSION 1
+
+/* Element type of logits and d_logits.  Outputs and saved rows are always fp32. */
+typedef enum k1_dtype {
+    K1_DTYPE_F32 = 0,
+    K1_DTYPE_F16 = 1,
+    K1_DTYPE_BF16 = 2
+} k1_dtype;
+
+typedef enum k1_status {
+    K1_OK = 0,
+    K1_ERR_INVALID_ARGUMENT = 1, /* bad size, stride, pointer or alignment */
+    K1_ERR_UNSUPPORTED_DTYPE = 2,
+    K1_ERR_WORKSPACE = 3,        /* workspace missing or smaller than required */
+    K1_ERR_CUDA = 4              /* a CUDA runtime call or kernel launch failed */
+} k1_status;
+
+/*
+ * Per-row partial state of one vocabulary shard (vocab-parallel mode).  Relative to
+ * the shard's own maximum m:  z = sum_v exp(x_v - m),  t = sum_v exp(x_v - m)(x_v - m).
+ * x_t is the target logit when the target column lies in this shard (has_target = 1).
+ * A shard whose columns are all -inf has m = -inf and z = t = 0.
+ * No counterpart in the reference (it has no multi-GPU path); the combine rule is the
+ * reference's (m, Z, T) merge (csrc/fused_logprob.cu:119-154) carried in fp64.
+ */
+typedef struct k1_partial {
+    double z;
+    double t;
+    float m;
+    float x_t;
+    int32_t has_target;
+    int32_t reserved;
+} k1_partial;
+
+/* Message describing the last failing call made by this thread ("" if none). */
+const char* k1_last_error(void);
+
+/* K1_ABI_VERSION of the loaded library. */
+int k1_abi_version(void);
+
+/*
+ * Device scratch needed by k1_fused_logprob_entropy_v1 and k1_vocab_shard_partials
+ * for the cross-CTA combine of rows that are split between thread blocks.  The
+ * workspace must be zero-filled before its first use; every call leaves it
+ * zero-filled again, so one buffer can be reused by consecutive calls on one stream.
+ * Calls that may overlap on the GPU need separate workspaces.  device = CUDA ordinal.
+ */
+size_t k1_forward_workspace_bytes(int64_t n_rows, int64_t vocab, int dtype, int device);
+
+/*
+ * Forward (production path).  Replaces fused_logprob_entropy_v1
+ * (reference csrc/fused_logprob.cu:355-403, bound at csrc/bindings.cpp:21-23).
+ *   logits   : rows x vocab elements of `dtype`, layout as described above
+ *   targets  : n_rows int64, contiguous
+ *   logprob, entropy, lse : n_rows fp32 each, contiguous (written)
+ * One streaming read of the logits; every thread block gets an equal share of the
+ * flattened row x vocab range, so few rows (split-vocab) and many rows use the same
+ * kernel.
+ */
+int k1_fused_logprob_entropy_v1(const void* logits, int dtype, int64_t n_rows, int64_t vocab,
+                                int64_t inner_rows, int64_t inner_stride, int64_t outer_stride,
+                                const int64_t* targets, float* logprob, float* entropy,
+                                float* lse, void* workspace, size_t workspace_bytes,
+                                void* stream);
+
+/*
+ * Forward, one thread per row, fp64 accumulation.  A simple correctness anchor,
+ * never fast.  Replaces fused_logprob_entropy_naive
+ * (reference csrc/fused_logprob.cu:405-458, bound at csrc/bindings.cpp:18-20).
+ */
+int k1_fused_logprob_entropy_naive(const void* logits, int dtype, int64_t n_rows, int64_t vocab,
+                                   int64_t inner_rows, int64_t inner_stride,
+                                   int64_t outer_stride, const int64_t* targets,
+                                   float* logprob, float* entropy, float* lse, void* stream);
+
+/*
+ * Backward.  Replaces fused_logprob_entropy_v1_backward
+ * (reference csrc/fused_logprob.cu:284-346, bound at csrc/bindings.cpp:24-26):
+ *   d_logits[r, v] = p (g_lse - g_logp - g_ent (x - lse + H)) + [v == t] g_logp,
+ *   p = exp(x - lse), using the forward's saved lse and entropy (fp32, n_rows each).
+ * g_logp / g_ent / g_lse may be NULL, meaning all-zero (the reference substitutes
+ * zero tensors in Python, python/kernel_opt/ops.py:71-76).
+ * d_logits has the dtype of logits and its own two-level row layout
+ * (d_inner_stride, d_outer_stride; same inner_rows); d_logits == logits with the same
+ * layout computes the gradient in place.
+ */
+int k1_fused_logprob_entropy_v1_backward(
+    const void* logits, int dtype, int64_t n_rows, int64_t vocab, int64_t inner_rows,
+    int64_t inner_stride, int64_t outer_stride, const int64_t* targets, const float* lse,
+    const float* entropy, const float* g_logp, const float* g_ent, const float* g_lse,
+    void* d_logits, int64_t d_inner_stride, int64_t d_outer_stride, void* stream);
+
+/*
+ * Vocab-parallel forward, step 1 of 3: per-row partial state of this rank's vocabulary
+ * shard, columns [vocab_offset, vocab_offset + shard_vocab) of the full vocabulary.
+ * `targets` hold global column ids.  partials: n_rows k1_partial (written).
+ * No counterpart in the reference (multi-GPU was out of its scope).
+ */
+int k1_vocab_shard_partials(const void* logits, int dtype, int64_t n_rows, int64_t shard_vocab,
+                            int64_t inner_rows, int64_t inner_stride, int64_t outer_stride,
+                            int64_t vocab_offset, const int64_t* targets,
+                            k1_partial* partials, void* workspace, size_t workspace_bytes,
+                            void* stream);
+
+/*
+ * Vocab-parallel forward, step 3 of 3 (step 2 is one all-gather of the partials):
+ * gathered = n_shards x n_rows k1_partial (shard-major) -> logprob, entropy, lse.
+ */
+int k1_vocab_combine(const k1_partial* gathered, int n_shards, int64_t n_rows,
+                     float* logprob, float* entropy, float* lse, void* stream);
+
+/*
+ * Vocab-parallel backward: the backward above restricted to this rank's shard, with
+ * the global lse / entropy of the combined forward.  The one-hot term is applied only
+ * where the global target falls inside [vocab_offset, vocab_offset + shard_vocab).
+ */
+int k1_vocab_shard_backward(
+    const void* logits, int dtype, int64_t n_rows, int64_t shard_vocab, int64_t inner_rows,
+    int64_t inner_stride, int64_t outer_stride, int64_t vocab_offset, const int64_t* targets,
+    const float* lse, const float* entropy, const float* g_logp, const float* g_ent,
+    const float* g_lse, void* d_logits, int64_t d_inner_stride, int64_t d_outer_stride,
+    void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* K1_LOGPROB_H */

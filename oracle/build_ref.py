@@ -1,0 +1,53 @@
+"""TEST INFRASTRUCTURE ONLY.  Build the reference's own K1 CUDA extension for sm_100a.
+
+Compiles the reference sources where they lie (csrc/bindings.cpp and
+csrc/fused_logprob.cu of the reference checkout; nothing is copied into this
+repository) with torch.utils.cpp_extension.load and the reference's own nvcc flags
+(setup.py:5-11: -O3 --use_fast_math -std=c++17), retargeted from sm_89 to sm_100a.
+The reference's setup.py is not used: its MSVC-only cxx flags do not work with gcc.
+Output: oracle/_ref/k1_reference*.so (git-ignored; it travels to the GPU box with the
+rest of the tree).  Used only by GPU tests to pin the oracle and the kernels against the
+reference kernels' actual outputs.
+"""
+from __future__ import annotations
+
+import glob
+import os
+import sys
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+OUT = os.path.join(HERE, "_ref")
+NAME = "k1_reference"
+DEFAULT_REF = os.environ.get("K1_REFERENCE_ROOT", "/root/reference")
+
+
+def built_path() -> str | None:
+    hits = sorted(glob.glob(os.path.join(OUT, NAME + "*.so")))
+    return hits[0] if hits else None
+
+
+def build(ref_root: str = DEFAULT_REF, force: bool = False) -> str | None:
+    srcs = [os.path.join(ref_root, "csrc", "bindings.cpp"),
+            os.path.join(ref_root, "csrc", "fused_logprob.cu")]
+    if not all(os.path.exists(s) for s in srcs):
+        return built_path()
+    have = built_path()
+    if have and not force and all(os.path.getmtime(have) >= os.path.getmtime(s) for s in srcs):
+        return have
+    os.makedirs(OUT, exist_ok=True)
+    os.environ["TORCH_CUDA_ARCH_LIST"] = "10.0a"
+    from torch.utils import cpp_extension
+    cpp_extension.load(
+        name=NAME,
+        sources=srcs,
+        extra_cflags=["-O3", "-std=c++17"],
+        extra_cuda_cflags=["-O3", "--use_fast_math", "-std=c++17"],
+        build_directory=OUT,
+        verbose=False,
+    )
+    return built_path()
+
+
+if __name__ == "__main__":
+    p = build(force="--force" in sys.argv)
+    print(p if p else "reference sources not found; nothing built")

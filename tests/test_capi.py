@@ -1,0 +1,93 @@
+"""The C-ABI library (libk1_b200.so) loads without a GPU, exports every function that
+include/k1_logprob.h declares, and rejects bad arguments before touching the device."""
+import ctypes
+
+import pytest
+
+from _helpers import CAPI_LIB, header_functions
+
+K1_OK, K1_ERR_INVALID, K1_ERR_DTYPE, K1_ERR_WS = 0, 1, 2, 3
+
+
+@pytest.fixture(scope="module")
+def lib():
+    return ctypes.CDLL(CAPI_LIB)
+
+
+def test_header_declares_expected_entry_points():
+    names = header_functions()
+    for n in ("k1_fused_logprob_entropy_v1", "k1_fused_logprob_entropy_naive",
+              "k1_fused_logprob_entropy_v1_backward", "k1_vocab_shard_partials",
+              "k1_vocab_combine", "k1_vocab_shard_backward", "k1_forward_workspace_bytes",
+              "k1_last_error", "k1_abi_version"):
+        assert n in names
+
+
+def test_every_declared_symbol_is_exported(lib):
+    missing = [n for n in header_functions() if not hasattr(lib, n)]
+    assert not missing, f"declared but not exported: {missing}"
+
+
+def test_abi_version(lib):
+    lib.k1_abi_version.restype = ctypes.c_int
+    assert lib.k1_abi_version() == 1
+
+
+def _fwd(lib, dtype=2, n_rows=4, vocab=16, inner_rows=4, inner_stride=16, outer=0,
+         logits=1024, targets=2048, out=4096, ws=8192, ws_bytes=1 << 20):
+    f = lib.k1_fused_logprob_entropy_v1
+    i64, p = ctypes.c_int64, ctypes.c_void_p
+    f.argtypes = [p, ctypes.c_int, i64, i64, i64, i64, i64, p, p, p, p, p, ctypes.c_size_t, p]
+    f.restype = ctypes.c_int
+    return f(logits, dtype, n_rows, vocab, inner_rows, inner_stride, outer, targets, out, out,
+             out, ws, ws_bytes, None)
+
+
+def _err(lib):
+    lib.k1_last_error.restype = ctypes.c_char_p
+    return lib.k1_last_error().decode()
+
+
+def test_rejects_bad_dtype(lib):
+    assert _fwd(lib, dtype=7) == K1_ERR_DTYPE
+    assert "bf16, fp16, or fp32" in _err(lib)
+
+
+def test_rejects_bad_shapes(lib):
+    assert _fwd(lib, vocab=0) == K1_ERR_INVALID
+    assert "vocab" in _err(lib)
+    assert _fwd(lib, n_rows=5, inner_rows=2) == K1_ERR_INVALID
+    assert "inner_rows" in _err(lib)
+    assert _fwd(lib, n_rows=-1) == K1_ERR_INVALID
+    assert _fwd(lib, inner_stride=-3) == K1_ERR_INVALID
+
+
+def test_rejects_null_and_misaligned_pointers(lib):
+    assert _fwd(lib, logits=0) == K1_ERR_INVALID
+    assert "NULL" in _err(lib)
+    assert _fwd(lib, logits=1025) == K1_ERR_INVALID  # bf16 needs 2-byte alignment
+    assert "aligned" in _err(lib)
+    assert _fwd(lib, targets=0) == K1_ERR_INVALID
+
+
+def test_zero_rows_is_a_no_op(lib):
+    assert _fwd(lib, n_rows=0, logits=0, targets=0, out=0, ws=0) == K1_OK
+
+
+def test_backward_and_combine_validation(lib):
+    i64, p, c_int = ctypes.c_int64, ctypes.c_void_p, ctypes.c_int
+    b = lib.k1_fused_logprob_entropy_v1_backward
+    b.argtypes = [p, c_int, i64, i64, i64, i64, i64, p, p, p, p, p, p, p, i64, i64, p]
+    b.restype = c_int
+    assert b(1024, 9, 4, 16, 4, 16, 0, 2048, 4096, 4096, None, None, None, 8192, 16, 0,
+             None) == K1_ERR_DTYPE
+    assert b(1024, 2, 4, 16, 4, 16, 0, 2048, 4096, 4096, None, None, None, 0, 16, 0,
+             None) == K1_ERR_INVALID
+    c = lib.k1_vocab_combine
+    c.argtypes = [p, c_int, i64, p, p, p, p]
+    c.restype = c_int
+    assert c(1024, 0, 4, 4096, 4096, 4096, None) == K1_ERR_INVALID
+    v = lib.k1_vocab_shard_partials
+    v.argtypes = [p, c_int, i64, i64, i64, i64, i64, i64, p, p, p, ctypes.c_size_t, p]
+    v.restype = c_int
+    assert v(1024, 2, 4, 16, 4, 16, 0, -5, 2048, 4096, 8192, 1 << 20, None) == K1_ERR_INVALID

@@ -1,0 +1,68 @@
+"""kernel_opt imports without a GPU (its native extension and C-ABI library load), keeps
+the reference's public surface, and reports bad input the way the reference does."""
+import pytest
+import torch
+
+import kernel_opt
+from kernel_opt import _C, grpo, parallel
+
+
+def test_public_surface_matches_reference():
+    # reference python/kernel_opt/__init__.py:1-15 and csrc/bindings.cpp:17-26
+    for name in ("fused_logprob_entropy", "fused_logprob_entropy_forward",
+                 "fused_logprob_entropy_naive"):
+        assert callable(getattr(kernel_opt, name))
+    for name in ("fused_logprob_entropy_naive", "fused_logprob_entropy_v1",
+                 "fused_logprob_entropy_v1_backward"):
+        assert callable(getattr(_C, name))
+    assert _C.abi_version() == 1
+
+
+def test_trainer_is_lazy():
+    with pytest.raises((ImportError, AttributeError)):
+        kernel_opt.KernelOptGRPOTrainer  # trl is not installed here
+    with pytest.raises(AttributeError):
+        kernel_opt.does_not_exist
+
+
+def test_native_libraries_are_the_in_tree_builds():
+    import os
+    maps = open("/proc/self/maps").read()
+    root = os.path.dirname(kernel_opt.__file__)
+    assert os.path.join(root, "lib", "libk1_b200.so") in maps
+    assert os.path.dirname(_C.__file__) == root
+
+
+def test_binding_errors_match_reference_messages():
+    x = torch.randn(2, 8)
+    t = torch.zeros(2, dtype=torch.int64)
+    o = torch.empty(2)
+    with pytest.raises(RuntimeError, match="logits must be CUDA"):
+        _C.fused_logprob_entropy_v1(x, t, o, o, o)
+    with pytest.raises(RuntimeError, match="logits dtype must be bf16, fp16, or fp32"):
+        _C.fused_logprob_entropy_v1(x.double(), t, o, o, o)
+    with pytest.raises(AssertionError):
+        kernel_opt.fused_logprob_entropy(x, t)  # python layer asserts CUDA, as the reference
+
+
+def test_row_and_vocab_shards_partition():
+    for n in (0, 1, 7, 16, 1025):
+        for w in (1, 2, 3, 8):
+            parts = [parallel.row_shard(n, w, r) for r in range(w)]
+            assert parts[0].start == 0 and parts[-1].stop == n
+            for a, b in zip(parts, parts[1:]):
+                assert a.stop == b.start
+            sizes = [s.stop - s.start for s in parts]
+            assert max(sizes) - min(sizes) <= 1
+    with pytest.raises(ValueError):
+        parallel.row_shard(10, 2, 2)
+    assert parallel.vocab_shard(256000, 8, 7) == slice(224000, 256000)
+
+
+def test_completion_window_is_a_strided_view():
+    base = torch.randn(3, 11, 5)
+    w = grpo.completion_window(base, 6)
+    assert w.shape == (3, 6, 5)
+    assert w.data_ptr() == base[:, 4:10].data_ptr()
+    assert w.stride() == (55, 5, 1) and not w.is_contiguous()
+    torch.testing.assert_close(w, base[:, :-1][:, -6:])
