@@ -14,7 +14,7 @@
 #include <string>
 #include <utility>
 
-#include "k1_kernels.cuh"
+#include "k1_ring.cuh"
 
 namespace {
 
@@ -38,7 +38,24 @@ int check_launch(const char* what) {
 }
 
 constexpr int kThreads = 256;
-constexpr int kUnroll = 8;           // 16-byte vectors in flight per thread and chunk
+constexpr int kUnroll = K1_FWD_UNROLL;      // 16-byte vectors per thread and chunk (forward)
+constexpr int kUnrollBwd = K1_BWD_UNROLL;   // 16-byte vectors per thread and chunk (backward)
+#ifndef K1_RING
+#define K1_RING 0
+#endif
+#ifndef K1_RING_WARPS
+#define K1_RING_WARPS 8
+#endif
+#ifndef K1_RING_STAGES
+#define K1_RING_STAGES 4
+#endif
+#ifndef K1_RING_BYTES
+#define K1_RING_BYTES 16384
+#endif
+constexpr bool kRing = K1_RING != 0;        // bulk-copy ring kernels on the vector path
+constexpr int kRingWarps = K1_RING_WARPS;   // consumer warps per block (+1 producer warp)
+constexpr int kRingStages = K1_RING_STAGES;
+constexpr int kRingBytes = K1_RING_BYTES;   // bytes per ring stage
 constexpr int kMaxDevices = 64;
 constexpr int kMaxBlocksPerSm = 8;   // grid cap used to size the workspace
 constexpr int64_t kMinUnitsPerBlockVec = (int64_t)kThreads * kUnroll;
@@ -66,9 +83,11 @@ int sm_count(int dev, int* out) {
     return K1_OK;
 }
 
-// Resident blocks per SM of one kernel instance, cached per (device, kernel).
+// Resident blocks per SM of one kernel instance, cached per (device, kernel).  Kernels
+// with more than 48 KB of dynamic shared memory get the opt-in attribute set here, once
+// per device.
 template <typename Kernel>
-int blocks_per_sm(Kernel kernel, int dev, int* out) {
+int blocks_per_sm(Kernel kernel, int dev, int threads, size_t smem, int* out) {
     static std::mutex mu;
     static std::map<std::pair<int, const void*>, int> cache;
     const auto key = std::make_pair(dev, reinterpret_cast<const void*>(kernel));
@@ -80,8 +99,14 @@ int blocks_per_sm(Kernel kernel, int dev, int* out) {
             return K1_OK;
         }
     }
+    cudaError_t e = cudaSuccess;
+    if (smem > 0) {
+        e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess)
+            return fail(K1_ERR_CUDA, "cudaFuncSetAttribute(smem): %s", cudaGetErrorString(e));
+    }
     int v = 0;
-    cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&v, kernel, kThreads, 0);
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&v, kernel, threads, smem);
     if (e != cudaSuccess) return fail(K1_ERR_CUDA, "occupancy query: %s", cudaGetErrorString(e));
     if (v < 1) v = 1;
     if (v > kMaxBlocksPerSm) v = kMaxBlocksPerSm;
@@ -130,11 +155,12 @@ size_t workspace_bytes_for(int sms) {
 }
 
 template <typename Kernel>
-int grid_for(Kernel kernel, int dev, int64_t total, int64_t min_units, int64_t* grid) {
+int grid_for(Kernel kernel, int dev, int64_t total, int64_t min_units, int64_t* grid,
+             int threads = kThreads, size_t smem = 0) {
     int sms = 0, occ = 0;
     int rc = sm_count(dev, &sms);
     if (rc) return rc;
-    rc = blocks_per_sm(kernel, dev, &occ);
+    rc = blocks_per_sm(kernel, dev, threads, smem, &occ);
     if (rc) return rc;
     int64_t g = (int64_t)sms * occ;
     int64_t need = (total + min_units - 1) / min_units;
@@ -224,13 +250,20 @@ int launch_backward(const char* fn, const void* logits, const Rows& L, const Row
     p.g_ent = g_ent;
     p.g_lse = g_lse;
     int64_t grid = 1;
-    if (vec) {
-        auto kern = k1::k1_bwd_kernel<T, kThreads, kUnroll, true>;
+    if (vec && kRing) {
+        auto kern = k1::k1_bwd_ring_kernel<T, kRingWarps, kRingStages, kRingBytes>;
+        const int threads = (kRingWarps + 1) * 32;
+        const size_t smem = (size_t)kRingStages * kRingBytes;
+        rc = grid_for(kern, dev, p.total, kMinUnitsPerBlockVec, &grid, threads, smem);
+        if (rc) return rc;
+        kern<<<(unsigned)grid, threads, smem, stream>>>(p);
+    } else if (vec) {
+        auto kern = k1::k1_bwd_kernel<T, kThreads, kUnrollBwd, true>;
         rc = grid_for(kern, dev, p.total, kMinUnitsPerBlockVec, &grid);
         if (rc) return rc;
         kern<<<(unsigned)grid, kThreads, 0, stream>>>(p);
     } else {
-        auto kern = k1::k1_bwd_kernel<T, kThreads, kUnroll, false>;
+        auto kern = k1::k1_bwd_kernel<T, kThreads, kUnrollBwd, false>;
         rc = grid_for(kern, dev, p.total, kMinUnitsPerBlockScalar, &grid);
         if (rc) return rc;
         kern<<<(unsigned)grid, kThreads, 0, stream>>>(p);
@@ -255,6 +288,17 @@ int check_common(const char* fn, const void* logits, int dtype, const Rows& L) {
 extern "C" {
 
 const char* k1_last_error(void) { return g_last_error.c_str(); }
+
+// Reads (and clears) the bulk-copy ring's timeout word on the current device; blocks
+// until prior work on the device finished.  0 = no bounded wait ran out.
+int k1_ring_status(unsigned* out) {
+    unsigned v = 0, zero = 0;
+    cudaError_t e = cudaMemcpyFromSymbol(&v, k1::k1_ring_error, sizeof v);
+    if (e == cudaSuccess) e = cudaMemcpyToSymbol(k1::k1_ring_error, &zero, sizeof zero);
+    if (e != cudaSuccess) return fail(K1_ERR_CUDA, "k1_ring_status: %s", cudaGetErrorString(e));
+    if (out) *out = v;
+    return K1_OK;
+}
 
 int k1_abi_version(void) { return K1_ABI_VERSION; }
 

@@ -49,16 +49,9 @@ __device__ __forceinline__ float fmax_nan(float a, float b) {
 __device__ __forceinline__ float2 add2(float2 a, float2 b) { return __fadd2_rn(a, b); }
 __device__ __forceinline__ float2 mul2(float2 a, float2 b) { return __fmul2_rn(a, b); }
 __device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) { return __ffma2_rn(a, b, c); }
-__device__ __forceinline__ float2 sub2(float2 a, float2 b) {
-    uint64_t ra, rb, rd;
-    asm("mov.b64 %0, {%1, %2};" : "=l"(ra) : "f"(a.x), "f"(a.y));
-    asm("mov.b64 %0, {%1, %2};" : "=l"(rb) : "f"(b.x), "f"(b.y));
-    asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(rd) : "l"(ra), "l"(rb));
-    float2 d;
-    asm("mov.b64 {%0, %1}, %2;" : "=f"(d.x), "=f"(d.y) : "l"(rd));
-    return d;
-}
 __device__ __forceinline__ float2 splat(float v) { return make_float2(v, v); }
+// a - b, exactly rounded (a single fma with -1).
+__device__ __forceinline__ float2 diff2(float2 a, float2 b) { return fma2(b, splat(-1.f), a); }
 
 // Streaming 16-byte load: read once, do not keep in L1.
 __device__ __forceinline__ uint4 ldg_stream(const void* p) {
@@ -113,6 +106,17 @@ struct DT<__nv_bfloat16> {
     }
     __device__ static __forceinline__ float clamp1(float x) { return fmax_nan(x, kLowest); }
 };
+
+// d = x - m for the two bf16 logits of w, without a separate conversion: the sm_100
+// mixed-precision add takes a bf16 operand and an fp32 operand.
+__device__ __forceinline__ float2 bf16x2_minus(uint32_t w, float nm) {
+    float d0, d1;
+    asm("{\n\t.reg .b16 lo, hi;\n\tmov.b32 {lo, hi}, %2;\n\t"
+        "add.rn.f32.bf16 %0, lo, %3;\n\tadd.rn.f32.bf16 %1, hi, %3;\n\t}"
+        : "=f"(d0), "=f"(d1)
+        : "r"(w), "f"(nm));
+    return make_float2(d0, d1);
+}
 
 template <>
 struct DT<__half> {
@@ -178,21 +182,29 @@ struct FwdState {
         t = mul2(fma2(splat(dl), z, t), s2);
         zb = mul2(zb, s2);
         zs = mul2(zs, s2);
-        float2 g = sub2(add2(zb, splat(kSplit)), splat(kSplit));
-        zs = add2(zs, sub2(zb, g));
+        float2 g = add2(add2(zb, splat(kSplit)), splat(-kSplit));
+        zs = add2(zs, diff2(zb, g));
         zb = g;
         m = mn;
     }
 
-    // Accumulate two clamped logits; nm = (-m, -m).
-    __device__ __forceinline__ void accum(float2 x, float2 nm) {
-        float2 d = add2(x, nm);
+    // Accumulate two logits given as d = x - m.
+    __device__ __forceinline__ void accum_d(float2 d) {
         float2 tt = mul2(d, splat(kLog2e));
         float2 e = make_float2(ex2(tt.x), ex2(tt.y));
-        float2 g = sub2(add2(e, splat(kSplit)), splat(kSplit));
+        float2 g = add2(add2(e, splat(kSplit)), splat(-kSplit));
         zb = add2(zb, g);
-        zs = add2(zs, sub2(e, g));
+        zs = add2(zs, diff2(e, g));
         t = fma2(e, d, t);
+    }
+
+    // Accumulate two logits; nm = (-m, -m).
+    __device__ __forceinline__ void accum(float2 x, float2 nm) { accum_d(add2(x, nm)); }
+
+    // true when a -inf logit met the fast (unclamped) path: e = 0 times d = -inf made t
+    // NaN while z stayed finite.  NaN logits poison z as well and are not flagged.
+    __device__ __forceinline__ bool saw_neg_inf() const {
+        return isnan(t.x + t.y) && !isnan(zb.x + zb.y + zs.x + zs.y) && !isnan(m);
     }
 };
 
@@ -220,6 +232,34 @@ __device__ __forceinline__ double warp_sum(double v) {
     return v;
 }
 
+// Barrier over the first THREADS threads of the block: the whole block (BAR = 0,
+// __syncthreads) or a named hardware barrier shared by those threads only (BAR > 0,
+// used when a producer warp does not take part).
+template <int THREADS, int BAR>
+__device__ __forceinline__ void group_sync() {
+    if constexpr (BAR == 0) {
+        __syncthreads();
+    } else {
+        asm volatile("bar.sync %0, %1;" ::"r"(BAR), "r"(THREADS) : "memory");
+    }
+}
+
+template <int THREADS, int BAR>
+__device__ __forceinline__ bool group_or(bool v) {
+    if constexpr (BAR == 0) {
+        return __syncthreads_or(v) != 0;
+    } else {
+        uint32_t r;
+        asm volatile(
+            "{\n\t.reg .pred pi, po;\n\tsetp.ne.u32 pi, %1, 0;\n\t"
+            "bar.red.or.pred po, %2, %3, pi;\n\tselp.u32 %0, 1, 0, po;\n\t}"
+            : "=r"(r)
+            : "r"((uint32_t)v), "r"(BAR), "r"(THREADS)
+            : "memory");
+        return r != 0;
+    }
+}
+
 // Shared scratch for one block reduction.
 template <int THREADS>
 struct ReduceSmem {
@@ -229,9 +269,9 @@ struct ReduceSmem {
 };
 
 // Merge every thread's (m, z, t) -- z, t relative to that thread's own m -- into the
-// block's state relative to the block maximum.  `empty` threads contribute nothing.
-// The result is valid in every thread.  Contains __syncthreads(): call uniformly.
-template <int THREADS>
+// group's state relative to the group maximum.  `empty` threads contribute nothing.
+// The result is valid in every thread.  Synchronises the group: call uniformly.
+template <int THREADS, int BAR = 0>
 __device__ __forceinline__ RowPartial block_merge(float m, double z, double t, bool empty,
                                                   ReduceSmem<THREADS>& sm) {
     constexpr int NW = THREADS / 32;
@@ -239,7 +279,7 @@ __device__ __forceinline__ RowPartial block_merge(float m, double z, double t, b
     float mm = empty ? -INFINITY : m;
     float wm = warp_max_nan(mm);
     if (lane == 0) sm.wmax[warp] = wm;
-    __syncthreads();
+    group_sync<THREADS, BAR>();
     float M = sm.wmax[0];
 #pragma unroll
     for (int i = 1; i < NW; ++i) M = fmax_nan(M, sm.wmax[i]);
@@ -256,7 +296,7 @@ __device__ __forceinline__ RowPartial block_merge(float m, double z, double t, b
         sm.wz[warp] = zc;
         sm.wt[warp] = tc;
     }
-    __syncthreads();
+    group_sync<THREADS, BAR>();
     RowPartial r;
     r.z = 0.0;
     r.t = 0.0;
@@ -271,7 +311,7 @@ __device__ __forceinline__ RowPartial block_merge(float m, double z, double t, b
         r.t = 0.0;
     }
     r.pad = 0.f;
-    __syncthreads();  // smem is reused by the caller's next reduction
+    group_sync<THREADS, BAR>();  // smem is reused by the caller's next reduction
     return r;
 }
 

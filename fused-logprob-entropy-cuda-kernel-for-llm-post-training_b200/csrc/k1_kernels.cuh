@@ -10,6 +10,8 @@
 // last block to arrive at its ticket; nobody waits.
 #pragma once
 
+#include <type_traits>
+
 #include "k1_common.cuh"
 #include "../../include/k1_logprob.h"
 
@@ -30,6 +32,7 @@ struct FwdParams {
     k1_partial* partials;  // shard mode output
     RowPartial* ws_part;   // 2 * gridDim.x slots
     unsigned* ws_ticket;   // gridDim.x counters, zero between calls
+    unsigned* ws_error;    // set to nonzero if a bounded wait ran out (bulk-copy ring)
 };
 
 struct BwdParams {
@@ -48,6 +51,7 @@ struct BwdParams {
     const float* g_logp;
     const float* g_ent;
     const float* g_lse;
+    unsigned* ws_error;  // set to nonzero if a bounded wait ran out (bulk-copy ring)
 };
 
 // Block that owns flattened unit u when `total` units are cut into G equal pieces
@@ -59,17 +63,41 @@ __device__ __forceinline__ int64_t block_of(int64_t u, int64_t total, int64_t G)
 // ---------------------------------------------------------------------------------
 // Forward: per-chunk work of one thread
 // ---------------------------------------------------------------------------------
-template <typename T, int U>
+// Build-time tuning knobs (defaults are the measured best on B200).
+#ifndef K1_FWD_UNROLL
+#define K1_FWD_UNROLL 8
+#endif
+#ifndef K1_BWD_UNROLL
+#define K1_BWD_UNROLL 8
+#endif
+#ifndef K1_FWD_MINB
+#define K1_FWD_MINB 3
+#endif
+#ifndef K1_BWD_MINB
+#define K1_BWD_MINB 4
+#endif
+#ifndef K1_PREFETCH
+#define K1_PREFETCH 0
+#endif
+#ifndef K1_MIXED_ADD
+#define K1_MIXED_ADD 0
+#endif
+
+// CLAMP = false is the fast path: logits are used as loaded.  A -inf logit then turns t
+// into NaN (0 * -inf), which the caller detects after the segment and re-streams the
+// segment with CLAMP = true, where every logit is first clamped to the lowest finite
+// value of its type.
+template <typename T, int U, bool CLAMP>
 __device__ __forceinline__ void fwd_chunk(const uint4 (&v)[U], FwdState& st) {
     using D = DT<T>;
     if constexpr (sizeof(T) == 2) {
         uint32_t w[4 * U];
 #pragma unroll
         for (int u = 0; u < U; ++u) {
-            w[4 * u + 0] = D::clamp2(v[u].x);
-            w[4 * u + 1] = D::clamp2(v[u].y);
-            w[4 * u + 2] = D::clamp2(v[u].z);
-            w[4 * u + 3] = D::clamp2(v[u].w);
+            w[4 * u + 0] = CLAMP ? D::clamp2(v[u].x) : v[u].x;
+            w[4 * u + 1] = CLAMP ? D::clamp2(v[u].y) : v[u].y;
+            w[4 * u + 2] = CLAMP ? D::clamp2(v[u].z) : v[u].z;
+            w[4 * u + 3] = CLAMP ? D::clamp2(v[u].w) : v[u].w;
         }
         uint32_t mx[4 * U];
 #pragma unroll
@@ -83,15 +111,21 @@ __device__ __forceinline__ void fwd_chunk(const uint4 (&v)[U], FwdState& st) {
         st.rescale(fmax_nan(mf.x, mf.y));
         const float2 nm = splat(-st.m);
 #pragma unroll
-        for (int i = 0; i < 4 * U; ++i) st.accum(D::to_f2(w[i]), nm);
+        for (int i = 0; i < 4 * U; ++i) {
+            if constexpr (K1_MIXED_ADD && std::is_same<T, __nv_bfloat16>::value) {
+                st.accum_d(bf16x2_minus(w[i], nm.x));
+            } else {
+                st.accum(D::to_f2(w[i]), nm);
+            }
+        }
     } else {
         float f[4 * U];
 #pragma unroll
         for (int u = 0; u < U; ++u) {
-            f[4 * u + 0] = D::clamp1(__uint_as_float(v[u].x));
-            f[4 * u + 1] = D::clamp1(__uint_as_float(v[u].y));
-            f[4 * u + 2] = D::clamp1(__uint_as_float(v[u].z));
-            f[4 * u + 3] = D::clamp1(__uint_as_float(v[u].w));
+            f[4 * u + 0] = CLAMP ? D::clamp1(__uint_as_float(v[u].x)) : __uint_as_float(v[u].x);
+            f[4 * u + 1] = CLAMP ? D::clamp1(__uint_as_float(v[u].y)) : __uint_as_float(v[u].y);
+            f[4 * u + 2] = CLAMP ? D::clamp1(__uint_as_float(v[u].z)) : __uint_as_float(v[u].z);
+            f[4 * u + 3] = CLAMP ? D::clamp1(__uint_as_float(v[u].w)) : __uint_as_float(v[u].w);
         }
         float mx[4 * U];
 #pragma unroll
@@ -108,23 +142,51 @@ __device__ __forceinline__ void fwd_chunk(const uint4 (&v)[U], FwdState& st) {
     }
 }
 
-// Stream vectors [j0, j1) of one row (vector path: row start 16-byte aligned and the
-// row an exact number of vectors).
-template <typename T, int THREADS, int U>
-__device__ __forceinline__ void fwd_stream_vec(const T* rowp, int64_t j0, int64_t j1,
-                                               FwdState& st) {
-    const uint4* vp = reinterpret_cast<const uint4*>(rowp);
-    int64_t j = j0 + threadIdx.x;
-    for (; j + (int64_t)(U - 1) * THREADS < j1; j += (int64_t)U * THREADS) {
-        uint4 v[U];
+template <int U, int THREADS>
+__device__ __forceinline__ void load_vectors(uint4 (&v)[U], const uint4* vp, int64_t j) {
 #pragma unroll
-        for (int u = 0; u < U; ++u) v[u] = ldg_stream(vp + j + (int64_t)u * THREADS);
-        fwd_chunk<T, U>(v, st);
+    for (int u = 0; u < U; ++u) v[u] = ldg_stream(vp + j + (int64_t)u * THREADS);
+}
+
+// Stream vectors [j0, j1) of one row (vector path: row start 16-byte aligned and the
+// row an exact number of vectors).  `tid` / THREADS: this thread's lane in the group
+// that shares the segment.  With K1_PREFETCH the next chunk's loads are issued before
+// the current chunk is reduced (two register buffers, used alternately).
+template <typename T, int THREADS, int U, bool CLAMP>
+__device__ __forceinline__ void fwd_stream_vec(const T* rowp, int64_t j0, int64_t j1,
+                                               FwdState& st, int tid) {
+    const uint4* vp = reinterpret_cast<const uint4*>(rowp);
+    constexpr int64_t kSpan = (int64_t)(U - 1) * THREADS;
+    constexpr int64_t kStep = (int64_t)U * THREADS;
+    int64_t j = j0 + tid;
+    if constexpr (K1_PREFETCH) {
+        if (j + kSpan < j1) {
+            uint4 a[U], b[U];
+            load_vectors<U, THREADS>(a, vp, j);
+            while (true) {
+                bool more = j + kStep + kSpan < j1;
+                if (more) load_vectors<U, THREADS>(b, vp, j + kStep);
+                fwd_chunk<T, U, CLAMP>(a, st);
+                j += kStep;
+                if (!more) break;
+                more = j + kStep + kSpan < j1;
+                if (more) load_vectors<U, THREADS>(a, vp, j + kStep);
+                fwd_chunk<T, U, CLAMP>(b, st);
+                j += kStep;
+                if (!more) break;
+            }
+        }
+    } else {
+        for (; j + kSpan < j1; j += kStep) {
+            uint4 v[U];
+            load_vectors<U, THREADS>(v, vp, j);
+            fwd_chunk<T, U, CLAMP>(v, st);
+        }
     }
     for (; j < j1; j += THREADS) {
         uint4 v[1];
         v[0] = ldg_stream(vp + j);
-        fwd_chunk<T, 1>(v, st);
+        fwd_chunk<T, 1, CLAMP>(v, st);
     }
 }
 
@@ -172,76 +234,204 @@ __device__ __forceinline__ void fwd_emit_row(const FwdParams& p, int64_t r, cons
     }
 }
 
+// Rows a block finishes are not written immediately: their merged state is parked in
+// shared memory and kRowCap rows are finalised at once, one row per thread (fp64 log and
+// divide, the target-logit load).  Doing it per row in one thread would stall that warp,
+// and with it the next block-wide barrier, once per row.
+constexpr int kRowCap = 32;
+
+template <int THREADS>
+struct FwdSmem {
+    static constexpr int NW = THREADS / 32;
+    float wmax[2][NW];   // per-warp maxima, double-buffered by segment parity
+    int wbad[2][NW];     // per-warp "saw -inf on the fast path"
+    double wz[2][NW];
+    double wt[2][NW];
+    ReduceSmem<THREADS> merge;  // split-row merges at the end of the block
+    RowPartial done_part[kRowCap];
+    int64_t done_row[kRowCap];
+    unsigned split_prev[2];  // ticket values of the block's first / last split row
+};
+
+// Merge the threads' states of one segment into `out` (relative to the segment maximum).
+// Returns false -- uniformly, after an extra barrier -- when some thread flagged `bad`; the
+// caller then re-streams the segment clamped and merges again.  Two barriers otherwise:
+// the scratch is double-buffered by segment parity, so no trailing barrier is needed.
+template <int THREADS, int BAR>
+__device__ __forceinline__ bool seg_merge(float m, double z, double t, bool empty, bool bad,
+                                          FwdSmem<THREADS>& sm, int buf, RowPartial& out) {
+    constexpr int NW = THREADS / 32;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const float wm = warp_max_nan(empty ? -INFINITY : m);
+    const bool wb = __any_sync(0xffffffffu, bad);
+    if (lane == 0) {
+        sm.wmax[buf][warp] = wm;
+        sm.wbad[buf][warp] = wb ? 1 : 0;
+    }
+    group_sync<THREADS, BAR>();
+    int any_bad = 0;
+    float M = sm.wmax[buf][0];
+#pragma unroll
+    for (int i = 0; i < NW; ++i) {
+        any_bad |= sm.wbad[buf][i];
+        M = fmax_nan(M, sm.wmax[buf][i]);
+    }
+    if (any_bad) {
+        group_sync<THREADS, BAR>();  // everyone has read the flags before the retry
+        return false;
+    }
+    double zc = 0.0, tc = 0.0;
+    if (!empty) {
+        const float dm = m - M;
+        const float sc = (dm == 0.f) ? 1.f : ex2(dm * kLog2e);
+        zc = (double)sc * z;
+        tc = (double)sc * (t + (double)dm * z);
+    }
+    zc = warp_sum(zc);
+    tc = warp_sum(tc);
+    if (lane == 0) {
+        sm.wz[buf][warp] = zc;
+        sm.wt[buf][warp] = tc;
+    }
+    group_sync<THREADS, BAR>();
+    out.z = 0.0;
+    out.t = 0.0;
+#pragma unroll
+    for (int i = 0; i < NW; ++i) {
+        out.z += sm.wz[buf][i];
+        out.t += sm.wt[buf][i];
+    }
+    out.m = M;
+    if (M == -INFINITY) out.z = out.t = 0.0;
+    out.pad = 0.f;
+    return true;
+}
+
+// Finalise the parked rows, one per thread.
+template <typename T, int THREADS, int BAR, bool SHARD>
+__device__ __forceinline__ void fwd_flush_rows(const FwdParams& p, FwdSmem<THREADS>& sm, int count) {
+    group_sync<THREADS, BAR>();
+    const int tid = threadIdx.x;
+    if (tid < count) {
+        const int64_t r = sm.done_row[tid];
+        fwd_emit_row<T, SHARD>(p, r, reinterpret_cast<const T*>(p.logits) + p.lay.offset(r),
+                               sm.done_part[tid]);
+    }
+    group_sync<THREADS, BAR>();
+}
+
+// Split row r (its vectors span blocks bf..bl): merge every block's published piece and
+// write the row.  Called by the block that drew the last ticket.
+template <typename T, int THREADS, int BAR, bool SHARD>
+__device__ __forceinline__ void fwd_merge_split_row(const FwdParams& p, int64_t r,
+                                                    ReduceSmem<THREADS>& sm) {
+    const int tid = threadIdx.x;
+    const int64_t G = gridDim.x;
+    const int64_t bf = block_of(r * p.vpr, p.total, G);
+    const int64_t bl = block_of((r + 1) * p.vpr - 1, p.total, G);
+    __threadfence();
+    RowPartial acc;
+    acc.z = 0.0;
+    acc.t = 0.0;
+    acc.m = -INFINITY;
+    acc.pad = 0.f;
+    for (int64_t c = bf + tid; c <= bl; c += THREADS) {
+        const int64_t fr = (c * p.total / G) / p.vpr;
+        const RowPartial* q = p.ws_part + 2 * c + (r == fr ? 0 : 1);
+        RowPartial qq;
+        qq.z = __ldcg(&q->z);
+        qq.t = __ldcg(&q->t);
+        qq.m = __ldcg(&q->m);
+        qq.pad = 0.f;
+        acc = merge_partials(acc, qq);
+    }
+    RowPartial tot = block_merge<THREADS, BAR>(acc.m, acc.z, acc.t, acc.m == -INFINITY, sm);
+    if (tid == 0) {
+        fwd_emit_row<T, SHARD>(p, r, reinterpret_cast<const T*>(p.logits) + p.lay.offset(r), tot);
+        p.ws_ticket[bf] = 0u;  // leave the workspace zeroed for the next call
+    }
+}
+
 template <typename T, int THREADS, int U, bool VEC, bool SHARD>
-__global__ void __launch_bounds__(THREADS) k1_fwd_kernel(FwdParams p) {
-    __shared__ ReduceSmem<THREADS> sm;
-    __shared__ int s_last;
+__global__ void __launch_bounds__(THREADS, K1_FWD_MINB) k1_fwd_kernel(FwdParams p) {
+    constexpr int BAR = 0;
+    __shared__ FwdSmem<THREADS> sm;
+    const int tid = threadIdx.x;
     const int64_t G = gridDim.x, b = blockIdx.x;
-    int64_t start = b * p.total / G;
+    const int64_t start0 = b * p.total / G;
     const int64_t end = (b + 1) * p.total / G;
+    int64_t start = start0;
     int64_t r = start / p.vpr;
     int64_t j0 = start - r * p.vpr;
     const int64_t first_row = r;
+    int64_t split_row[2] = {-1, -1};
+    unsigned split_prev[2] = {0u, 0u};  // thread 0 only; read after the loop
+    int count = 0, buf = 0;
 
     while (start < end) {
         const int64_t j1 = min(p.vpr, j0 + (end - start));
         const T* rowp = reinterpret_cast<const T*>(p.logits) + p.lay.offset(r);
         FwdState st;
         st.init();
+        RowPartial part;
         if constexpr (VEC) {
-            fwd_stream_vec<T, THREADS, U>(rowp, j0, j1, st);
+            fwd_stream_vec<T, THREADS, U, false>(rowp, j0, j1, st, tid);
+            const double z = ((double)st.zb.x + (double)st.zb.y) + ((double)st.zs.x + (double)st.zs.y);
+            const double t = (double)st.t.x + (double)st.t.y;
+            if (!seg_merge<THREADS, BAR>(st.m, z, t, st.m <= DT<T>::kLowest, st.saw_neg_inf(), sm,
+                                         buf, part)) {
+                // rare: the segment holds -inf logits; stream it again, clamped
+                st.init();
+                fwd_stream_vec<T, THREADS, U, true>(rowp, j0, j1, st, tid);
+                const double z2 = ((double)st.zb.x + (double)st.zb.y) + ((double)st.zs.x + (double)st.zs.y);
+                const double t2 = (double)st.t.x + (double)st.t.y;
+                seg_merge<THREADS, BAR>(st.m, z2, t2, st.m <= DT<T>::kLowest, false, sm, buf, part);
+            }
         } else {
             fwd_stream_scalar<T, THREADS>(rowp, j0, j1, st);
+            const double z = ((double)st.zb.x + (double)st.zb.y) + ((double)st.zs.x + (double)st.zs.y);
+            const double t = (double)st.t.x + (double)st.t.y;
+            seg_merge<THREADS, BAR>(st.m, z, t, st.m <= DT<T>::kLowest, false, sm, buf, part);
         }
-        const bool empty = st.m <= DT<T>::kLowest;  // false for NaN
-        const double z = ((double)st.zb.x + (double)st.zb.y) + ((double)st.zs.x + (double)st.zs.y);
-        const double t = (double)st.t.x + (double)st.t.y;
-        RowPartial part = block_merge<THREADS>(st.m, z, t, empty, sm);
-
+        buf ^= 1;
         if (j0 == 0 && j1 == p.vpr) {
-            if (threadIdx.x == 0) fwd_emit_row<T, SHARD>(p, r, rowp, part);
+            if (tid == 0) {
+                sm.done_row[count] = r;
+                sm.done_part[count] = part;
+            }
+            if (++count == kRowCap) {
+                fwd_flush_rows<T, THREADS, BAR, SHARD>(p, sm, count);
+                count = 0;
+            }
         } else {
-            // Row shared with neighbouring blocks: publish this block's piece, and the
-            // last block to arrive merges all pieces.
-            const int64_t bf = block_of(r * p.vpr, p.total, G);
-            const int64_t bl = block_of((r + 1) * p.vpr - 1, p.total, G);
-            if (threadIdx.x == 0) {
-                RowPartial* slot = p.ws_part + 2 * b + (r == first_row ? 0 : 1);
-                *slot = part;
+            // Row shared with neighbouring blocks: publish this block's piece and draw a
+            // ticket; the block that draws the last one merges the row after its own loop.
+            const int slot = (r == first_row) ? 0 : 1;
+            split_row[slot] = r;
+            if (tid == 0) {
+                p.ws_part[2 * b + slot] = part;
                 __threadfence();
-                const unsigned prev = atomicAdd(p.ws_ticket + bf, 1u);
-                s_last = (prev == (unsigned)(bl - bf)) ? 1 : 0;
+                const int64_t bf = block_of(r * p.vpr, p.total, G);
+                split_prev[slot] = atomicAdd(p.ws_ticket + bf, 1u);
             }
-            __syncthreads();
-            if (s_last) {
-                __threadfence();
-                RowPartial acc;
-                acc.z = 0.0;
-                acc.t = 0.0;
-                acc.m = -INFINITY;
-                acc.pad = 0.f;
-                for (int64_t c = bf + threadIdx.x; c <= bl; c += THREADS) {
-                    const int64_t fr = (c * p.total / G) / p.vpr;
-                    const RowPartial* q = p.ws_part + 2 * c + (r == fr ? 0 : 1);
-                    RowPartial qq;
-                    qq.z = __ldcg(&q->z);
-                    qq.t = __ldcg(&q->t);
-                    qq.m = __ldcg(&q->m);
-                    qq.pad = 0.f;
-                    acc = merge_partials(acc, qq);
-                }
-                RowPartial tot = block_merge<THREADS>(acc.m, acc.z, acc.t,
-                                                      acc.m == -INFINITY, sm);
-                if (threadIdx.x == 0) {
-                    fwd_emit_row<T, SHARD>(p, r, rowp, tot);
-                    p.ws_ticket[bf] = 0u;  // leave the workspace zeroed for the next call
-                }
-            }
-            __syncthreads();
         }
         start += j1 - j0;
         ++r;
         j0 = 0;
+    }
+    if (tid == 0) {
+        sm.split_prev[0] = split_prev[0];
+        sm.split_prev[1] = split_prev[1];
+    }
+    fwd_flush_rows<T, THREADS, BAR, SHARD>(p, sm, count);  // its barrier publishes split_prev
+#pragma unroll
+    for (int slot = 0; slot < 2; ++slot) {
+        const int64_t sr = split_row[slot];
+        if (sr < 0) continue;
+        const int64_t bf = block_of(sr * p.vpr, p.total, G);
+        const int64_t bl = block_of((sr + 1) * p.vpr - 1, p.total, G);
+        if (sm.split_prev[slot] == (unsigned)(bl - bf))
+            fwd_merge_split_row<T, THREADS, BAR, SHARD>(p, sr, sm.merge);
     }
 }
 
@@ -325,7 +515,7 @@ __device__ __forceinline__ uint4 vec_set(uint4 o, int k, float val) {
 }
 
 template <typename T, int THREADS, int U, bool VEC>
-__global__ void __launch_bounds__(THREADS) k1_bwd_kernel(BwdParams p) {
+__global__ void __launch_bounds__(THREADS, K1_BWD_MINB) k1_bwd_kernel(BwdParams p) {
     using D = DT<T>;
     constexpr int EPV = VEC ? D::kEPV : 1;
     const int64_t G = gridDim.x, b = blockIdx.x;
@@ -353,19 +543,42 @@ __global__ void __launch_bounds__(THREADS) k1_bwd_kernel(BwdParams p) {
         if constexpr (VEC) {
             const uint4* xv = reinterpret_cast<const uint4*>(xr);
             uint4* dv = reinterpret_cast<uint4*>(dr);
+            constexpr int64_t kSpan = (int64_t)(U - 1) * THREADS;
+            constexpr int64_t kStep = (int64_t)U * THREADS;
             int64_t j = j0 + threadIdx.x;
-            for (; j + (int64_t)(U - 1) * THREADS < j1; j += (int64_t)U * THREADS) {
-                uint4 v[U];
-#pragma unroll
-                for (int u = 0; u < U; ++u) v[u] = ldg_stream(xv + j + (int64_t)u * THREADS);
+            auto emit = [&](const uint4(&v)[U], int64_t jb) {
 #pragma unroll
                 for (int u = 0; u < U; ++u) {
-                    const int64_t jj = j + (int64_t)u * THREADS;
+                    const int64_t jj = jb + (int64_t)u * THREADS;
                     uint4 o = bwd_vector<T>(v[u], q);
                     const uint64_t k = (uint64_t)(q.tl - jj * EPV);
                     if (k < (uint64_t)EPV)
                         o = vec_set<T>(o, (int)k, bwd_target_value(D::load1(xr + q.tl), q));
                     stg_stream(dv + jj, o);
+                }
+            };
+            if constexpr (K1_PREFETCH) {
+                if (j + kSpan < j1) {
+                    uint4 a[U], b[U];
+                    load_vectors<U, THREADS>(a, xv, j);
+                    while (true) {
+                        bool more = j + kStep + kSpan < j1;
+                        if (more) load_vectors<U, THREADS>(b, xv, j + kStep);
+                        emit(a, j);
+                        j += kStep;
+                        if (!more) break;
+                        more = j + kStep + kSpan < j1;
+                        if (more) load_vectors<U, THREADS>(a, xv, j + kStep);
+                        emit(b, j);
+                        j += kStep;
+                        if (!more) break;
+                    }
+                }
+            } else {
+                for (; j + kSpan < j1; j += kStep) {
+                    uint4 v[U];
+                    load_vectors<U, THREADS>(v, xv, j);
+                    emit(v, j);
                 }
             }
             for (; j < j1; j += THREADS) {
@@ -382,10 +595,12 @@ __global__ void __launch_bounds__(THREADS) k1_bwd_kernel(BwdParams p) {
                 if (j == q.tl) {
                     g = bwd_target_value(xraw, q);
                 } else {
+                    // the packed path's operations one lane at a time, so both paths
+                    // produce identical bits
                     const float x = D::clamp1(xraw);
-                    const float d = x - q.lse;
-                    const float pp = ex2(d * kLog2e);
-                    g = pp * q.c0 - q.ge * (pp * d);
+                    const float d = __fadd_rn(x, -q.lse);
+                    const float pp = ex2(__fmul_rn(d, kLog2e));
+                    g = __fmaf_rn(-q.ge, __fmul_rn(pp, d), __fmul_rn(pp, q.c0));
                 }
                 D::store1(dr + j, g);
             }

@@ -1,0 +1,204 @@
+// k1_ring.cuh -- bulk-copy (TMA) ring variant of the backward kernel.
+//
+// One producer warp per block streams the block's rows in chunks of up to SBYTES with
+// cp.async.bulk (global -> shared, completion counted on an mbarrier) into a ring of
+// STAGES buffers; NCW consumer warps transform and store straight out of shared memory,
+// then release the buffer on a second mbarrier.  The
+// number of bytes in flight per SM is set by the ring size, not by registers.
+//
+// Every mbarrier wait is bounded (kMaxTries polls with a suspend hint, a few seconds in
+// all).  A wait that runs out sets the device word k1_ring_error and the thread stops
+// waiting; the producer drains every copy it issued before it exits.  No wait depends
+// on another block or another GPU.  Bulk copies are plain global -> shared copies of this
+// GPU's memory (no multicast); source and size are multiples of 16 bytes on the vector
+// path.
+#pragma once
+
+#include "k1_kernels.cuh"
+
+#ifndef K1_RING_MINB
+#define K1_RING_MINB 1
+#endif
+
+namespace k1 {
+
+__device__ unsigned k1_ring_error;
+
+namespace ring {
+
+constexpr int kMaxTries = 4096;           // x up to 1 ms suspend hint per poll
+constexpr uint32_t kSuspendHintNs = 1000000;
+
+__device__ __forceinline__ uint32_t saddr(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ void bar_init(uint64_t* b, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(saddr(b)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void fence_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+__device__ __forceinline__ void arrive_expect(uint64_t* b, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(saddr(b)),
+                 "r"(bytes)
+                 : "memory");
+}
+__device__ __forceinline__ void arrive(uint64_t* b) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(saddr(b)) : "memory");
+}
+__device__ __forceinline__ bool try_wait(uint64_t* b, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(saddr(b)), "r"(parity), "r"(kSuspendHintNs)
+        : "memory");
+    return ok != 0;
+}
+// Bounded wait for the phase of parity `parity`; false (and the error word set) if it
+// did not complete in time.
+__device__ __forceinline__ bool wait(uint64_t* b, uint32_t parity) {
+    for (int i = 0; i < kMaxTries; ++i)
+        if (try_wait(b, parity)) return true;
+    atomicOr(&k1_ring_error, 1u);
+    return false;
+}
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::
+            "r"(saddr(dst)),
+        "l"(src), "r"(bytes), "r"(saddr(bar))
+        : "memory");
+}
+
+// The chunk sequence of one block: its flattened vector range [start, end) walked row by
+// row, each row segment cut into chunks of at most SV vectors.  Producer and consumers
+// walk the same sequence.
+struct ChunkWalk {
+    int64_t pos, end, r, j0, j1;
+    __device__ __forceinline__ void begin(int64_t start, int64_t stop, int64_t vpr) {
+        pos = start;
+        end = stop;
+        r = start / vpr;
+        j0 = start - r * vpr;
+        j1 = min(vpr, j0 + (end - pos));
+    }
+    __device__ __forceinline__ void next_row(int64_t vpr) {
+        pos += j1 - j0;
+        ++r;
+        j0 = 0;
+        j1 = min(vpr, end - pos);
+    }
+};
+
+// Producer: issue every chunk of the block, SBYTES at most each, into the ring.
+template <int STAGES, int SV>
+__device__ __forceinline__ void produce(const void* base, const RowLayout& lay, int es,
+                                        int64_t vpr, int64_t start, int64_t end, uint4* ring,
+                                        uint64_t* full, uint64_t* empty) {
+    ChunkWalk w;
+    w.begin(start, end, vpr);
+    uint32_t k = 0;
+    bool ok = true;
+    while (ok && w.pos < w.end) {
+        const uint4* src = reinterpret_cast<const uint4*>(reinterpret_cast<const char*>(base) +
+                                                          lay.offset(w.r) * es);
+        for (int64_t jj = w.j0; jj < w.j1; jj += SV) {
+            const uint32_t n = (uint32_t)min((int64_t)SV, w.j1 - jj);
+            const uint32_t s = k % STAGES, use = k / STAGES;
+            if (use > 0 && !wait(&empty[s], (use - 1) & 1)) {
+                ok = false;
+                break;
+            }
+            arrive_expect(&full[s], n * 16u);
+            bulk_g2s(ring + (size_t)s * SV, src + jj, n * 16u, &full[s]);
+            ++k;
+        }
+        w.next_row(vpr);
+    }
+    // drain: every issued copy has landed before this thread returns
+    for (uint32_t i = (k > (uint32_t)STAGES ? k - STAGES : 0u); i < k; ++i)
+        wait(&full[i % STAGES], (i / STAGES) & 1);
+}
+
+}  // namespace ring
+
+template <typename T, int NCW, int STAGES, int SBYTES>
+__global__ void __launch_bounds__((NCW + 1) * 32, K1_RING_MINB) k1_bwd_ring_kernel(BwdParams p) {
+    using D = DT<T>;
+    constexpr int NC = NCW * 32;
+    constexpr int SV = SBYTES / 16;
+    constexpr int VPT = SV / NC;
+    constexpr int EPV = D::kEPV;
+    static_assert(SV % NC == 0, "stage must hold a whole number of vectors per consumer");
+    extern __shared__ __align__(128) uint4 ring_buf[];
+    __shared__ __align__(8) uint64_t full[STAGES];
+    __shared__ __align__(8) uint64_t empty[STAGES];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; ++s) {
+            ring::bar_init(&full[s], 1);
+            ring::bar_init(&empty[s], NCW);
+        }
+        ring::fence_init();
+    }
+    __syncthreads();
+    const int64_t G = gridDim.x, b = blockIdx.x;
+    const int64_t start = b * p.total / G, end = (b + 1) * p.total / G;
+    if (warp == NCW) {
+        if (lane == 0)
+            ring::produce<STAGES, SV>(p.logits, p.lay, (int)sizeof(T), p.vpr, start, end, ring_buf,
+                                      full, empty);
+        return;
+    }
+    const int tid = threadIdx.x;
+    ring::ChunkWalk w;
+    w.begin(start, end, p.vpr);
+    uint32_t k = 0;
+    bool ok = true;
+    while (w.pos < w.end) {
+        const int64_t r = w.r;
+        const T* xr = reinterpret_cast<const T*>(p.logits) + p.lay.offset(r);
+        uint4* dv = reinterpret_cast<uint4*>(reinterpret_cast<T*>(p.dlogits) + p.dlay.offset(r));
+        BwdRow q;
+        q.lse = p.lse[r];
+        q.ent = p.entropy[r];
+        q.gl = p.g_logp ? p.g_logp[r] : 0.f;
+        q.ge = p.g_ent ? p.g_ent[r] : 0.f;
+        q.gs = p.g_lse ? p.g_lse[r] : 0.f;
+        q.c0 = q.gs - q.gl - q.ge * q.ent;
+        {
+            const int64_t tg = p.targets[r];
+            const int64_t tl = tg - p.col_offset;
+            q.tl = (tg >= 0 && tl >= 0 && tl < p.vocab) ? tl : -1;
+        }
+        for (int64_t jj = w.j0; jj < w.j1; jj += SV) {
+            const int64_t n = min((int64_t)SV, w.j1 - jj);
+            const uint32_t s = k % STAGES, use = k / STAGES;
+            if (ok) ok = ring::wait(&full[s], use & 1);
+            const uint4* stage = ring_buf + (size_t)s * SV;
+            if (ok) {
+#pragma unroll
+                for (int u = 0; u < VPT; ++u) {
+                    const int64_t i = tid + u * NC;
+                    if (i < n) {
+                        const int64_t jv = jj + i;
+                        uint4 o = bwd_vector<T>(stage[i], q);
+                        const uint64_t kk = (uint64_t)(q.tl - jv * EPV);
+                        if (kk < (uint64_t)EPV)
+                            o = vec_set<T>(o, (int)kk, bwd_target_value(D::load1(xr + q.tl), q));
+                        stg_stream(dv + jv, o);
+                    }
+                }
+            }
+            __syncwarp();
+            if (lane == 0) ring::arrive(&empty[s]);
+            ++k;
+        }
+        w.next_row(p.vpr);
+    }
+}
+
+}  // namespace k1

@@ -203,21 +203,28 @@ void backward_common(const char* which, at::Tensor logits, at::Tensor targets, i
     const float* ge = opt_grad(g_ent, L.n_rows, logits);
     const float* gs = opt_grad(g_lse, L.n_rows, logits);
     if (L.n_rows == 0) return;
-    // d_logits is addressed with the logits' row grouping: view it as
-    // [n_rows / inner_rows, inner_rows, V] (no copy) and read its two row strides.
+    // logits and d_logits share one row grouping (inner_rows): try the grouping of each
+    // tensor, view both as [n_rows / k, k, V] (no copy) and read their row strides.
     TORCH_CHECK(d_logits.size(-1) == 1 || d_logits.stride(-1) == 1,
                 "d_logits must be contiguous along the vocab dimension");
-    Rows D = L;
-    {
-        at::Tensor dv;
+    Rows D = logits_rows(d_logits);
+    bool found = false;
+    for (int64_t k : {L.inner_rows, D.inner_rows}) {
+        if (k < 1 || L.n_rows % k != 0) continue;
         try {
-            dv = d_logits.view({L.n_rows / L.inner_rows, L.inner_rows, L.vocab});
+            at::Tensor lv = logits.view({L.n_rows / k, k, L.vocab});
+            at::Tensor dv = d_logits.view({L.n_rows / k, k, L.vocab});
+            L.inner_rows = D.inner_rows = k;
+            L.inner_stride = lv.stride(1);
+            L.outer_stride = lv.stride(0);
+            D.inner_stride = dv.stride(1);
+            D.outer_stride = dv.stride(0);
+            found = true;
+            break;
         } catch (const c10::Error&) {
-            TORCH_CHECK(false, "d_logits layout cannot be addressed with the logits' row grouping");
         }
-        D.inner_stride = dv.stride(1);
-        D.outer_stride = dv.stride(0);
     }
+    TORCH_CHECK(found, "d_logits layout cannot be addressed with the logits' row grouping");
     c10::cuda::CUDAGuard guard(logits.device());
     cudaStream_t s = at::cuda::getCurrentCUDAStream().stream();
     int rc;

@@ -5,7 +5,7 @@ import pytest
 import torch
 
 import kernel_opt
-from _gpu import check_grad, grads_like, seeded_logits, seeded_targets
+from _gpu import GRAD_FLOOR, GRAD_RTOL, check_grad, grads_like, seeded_logits, seeded_targets
 from _helpers import assert_close_nan, golden_cases
 from kernel_opt import _C
 from oracle import oracle
@@ -31,10 +31,10 @@ def test_golden_cases(name):
     g = tuple(torch.from_numpy(c[k]).float() for k in ("g_logp", "g_ent", "g_lse"))
     d = autograd_grad(c["logits"], c["targets_t"], g)
     dt = c["logits"].dtype
-    rtol = 1e-5 if dt == torch.float32 else 1e-2
     ref = c["d_logits"]
     scale = np.abs(ref[np.isfinite(ref)]).max()
-    assert_close_nan(d.cpu().double().numpy(), ref, 1e-7 * scale, rtol, name)
+    atol = max(1e-7 * scale, GRAD_FLOOR[dt])
+    assert_close_nan(d.cpu().double().numpy(), ref, atol, GRAD_RTOL[dt], name)
 
 
 @pytest.mark.parametrize("dtype", DTYPES)
