@@ -41,7 +41,10 @@ constexpr int kThreads = 256;
 constexpr int kUnroll = K1_FWD_UNROLL;      // 16-byte vectors per thread and chunk (forward)
 constexpr int kUnrollBwd = K1_BWD_UNROLL;   // 16-byte vectors per thread and chunk (backward)
 #ifndef K1_RING
-#define K1_RING 0
+#define K1_RING 1
+#endif
+#ifndef K1_RING_FWD
+#define K1_RING_FWD 0
 #endif
 #ifndef K1_RING_WARPS
 #define K1_RING_WARPS 8
@@ -52,7 +55,8 @@ constexpr int kUnrollBwd = K1_BWD_UNROLL;   // 16-byte vectors per thread and ch
 #ifndef K1_RING_BYTES
 #define K1_RING_BYTES 16384
 #endif
-constexpr bool kRing = K1_RING != 0;        // bulk-copy ring kernels on the vector path
+constexpr bool kRing = K1_RING != 0;        // bulk-copy ring backward on the vector path
+constexpr bool kRingFwd = K1_RING_FWD != 0; // bulk-copy ring forward on the vector path
 constexpr int kRingWarps = K1_RING_WARPS;   // consumer warps per block (+1 producer warp)
 constexpr int kRingStages = K1_RING_STAGES;
 constexpr int kRingBytes = K1_RING_BYTES;   // bytes per ring stage
@@ -209,7 +213,14 @@ int launch_forward(const char* fn, const void* logits, const Rows& L, int64_t co
     p.ws_ticket = reinterpret_cast<unsigned*>(reinterpret_cast<char*>(workspace) +
                                               2 * gmax * sizeof(k1::RowPartial));
     int64_t grid = 1;
-    if (vec) {
+    if (vec && kRingFwd) {
+        auto kern = k1::k1_fwd_ring_kernel<T, kRingWarps, kRingStages, kRingBytes, SHARD>;
+        const int threads = (kRingWarps + 1) * 32;
+        const size_t smem = (size_t)kRingStages * kRingBytes;
+        rc = grid_for(kern, dev, p.total, kMinUnitsPerBlockVec, &grid, threads, smem);
+        if (rc) return rc;
+        kern<<<(unsigned)grid, threads, smem, stream>>>(p);
+    } else if (vec) {
         auto kern = k1::k1_fwd_kernel<T, kThreads, kUnroll, true, SHARD>;
         rc = grid_for(kern, dev, p.total, kMinUnitsPerBlockVec, &grid);
         if (rc) return rc;

@@ -7,13 +7,14 @@
 // state once per chunk, and then spends exactly one ex2 per element.  Arithmetic uses
 // the Blackwell packed f32x2 add / mul / fma, two logits per instruction.
 //
-// Precision.  Z = sum exp(x - m) is kept as two fp32 pairs: `zb` holds each term
-// rounded to a multiple of 2^-10 (exact while the sum stays below 2^14) and `zs` the
-// remainder.  For a near-one-hot row (one logit far above the rest) the maximum's term
-// is exactly 1 and lands in zb, while every tail term lands in zs with full relative
-// precision; a single fp32 accumulator would round the tail away and lose the
-// entropy.  T = sum exp(x - m)(x - m) is a sum of non-positive terms, so it never
-// cancels.  Thread and block states are merged in fp64.
+// Precision.  Z = sum exp(x - m) is kept as (count of logits equal to the running
+// maximum) + (fp32 sum of the other terms).  A compare masks the maximum's own term (d =
+// x - m is exactly 0 there) out of the fp32 sum, so for a near-one-hot row the tail keeps
+// its full relative precision; a plain fp32 Z would be 1 + tail and round the tail (and
+// with it the entropy) away.  Terms that only become "rest" when the maximum later moves
+// are folded in scaled by exp(m_old - m_new), where a dominant new maximum makes them
+// negligible and a close one makes the entropy large.  T = sum exp(x - m)(x - m) is a
+// sum of non-positive terms, so it never cancels.  Thread and block states merge in fp64.
 #pragma once
 
 #include <cuda_bf16.h>
@@ -24,8 +25,6 @@
 namespace k1 {
 
 constexpr float kLog2e = 1.4426950408889634f;
-// (e + kSplit) - kSplit rounds e in [0, 1] to a multiple of 2^-10.
-constexpr float kSplit = 8192.0f;
 // fp32 logits are clamped to this before use, so x - m stays finite for x = -inf.
 constexpr float kClampF32 = -1.0e38f;
 
@@ -35,6 +34,13 @@ constexpr float kClampF32 = -1.0e38f;
 __device__ __forceinline__ float ex2(float x) {
     float y;
     asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+// 1.0f where d != 0 or d is NaN, else 0.0f.
+__device__ __forceinline__ float not_zero(float d) {
+    float y;
+    asm("set.neu.f32.f32 %0, %1, 0f00000000;" : "=f"(y) : "f"(d));
     return y;
 }
 
@@ -80,6 +86,7 @@ struct DT<__nv_bfloat16> {
     static constexpr int kEPV = 8;
     static constexpr uint32_t kLowest2 = 0xFF7FFF7Fu;  // lowest finite bf16, both halves
     static constexpr float kLowest = -3.38953138925153547590470800371487866880e38f;
+    static constexpr uint32_t kPadWord = kLowest2;  // vector padding: contributes e = 0
     __device__ static __forceinline__ uint32_t clamp2(uint32_t w) {
         uint32_t r;
         asm("max.NaN.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(w), "r"(kLowest2));
@@ -123,6 +130,7 @@ struct DT<__half> {
     static constexpr int kEPV = 8;
     static constexpr uint32_t kLowest2 = 0xFBFFFBFFu;  // -65504, both halves
     static constexpr float kLowest = -65504.0f;
+    static constexpr uint32_t kPadWord = kLowest2;
     __device__ static __forceinline__ uint32_t clamp2(uint32_t w) {
         uint32_t r;
         asm("max.NaN.f16x2 %0, %1, %2;" : "=r"(r) : "r"(w), "r"(kLowest2));
@@ -151,6 +159,7 @@ template <>
 struct DT<float> {
     static constexpr int kEPV = 4;
     static constexpr float kLowest = kClampF32;
+    static constexpr uint32_t kPadWord = 0xFE967699u;  // bits of -1.0e38f
     __device__ static __forceinline__ float load1(const float* p) { return *p; }
     __device__ static __forceinline__ void store1(float* p, float v) { *p = v; }
     __device__ static __forceinline__ float clamp1(float x) { return fmax_nan(x, kClampF32); }
@@ -160,51 +169,64 @@ struct DT<float> {
 // Forward streaming state of one thread (see the header comment).
 // ---------------------------------------------------------------------------------
 struct FwdState {
-    float m;     // running maximum (clamped logits); <= kLowest of the type means "empty"
-    float2 zb;   // sum of exp(x - m) rounded to multiples of 2^-10
-    float2 zs;   // remainders
-    float2 t;    // sum of exp(x - m) * (x - m)
+    float m;    // running maximum (clamped logits); <= kLowest of the type means "empty"
+    float np;   // logits per lane since the running maximum last moved
+    float2 zs;  // sum of exp(x - m) over logits below the running maximum
+    float2 ms;  // number of logits below the running maximum since it last moved
+    float2 t;   // sum of exp(x - m) * (x - m)
 
     __device__ __forceinline__ void init() {
         m = -3.402823466e38f;
-        zb = splat(0.f);
+        np = 0.f;
         zs = splat(0.f);
+        ms = splat(0.f);
         t = splat(0.f);
     }
 
+    // Logits equal to the running maximum, per lane.
+    __device__ __forceinline__ float2 at_max() const { return make_float2(np - ms.x, np - ms.y); }
+
     // Move the reference point to max(m, mc).  Exact no-op when the maximum is unchanged.
     __device__ __forceinline__ void rescale(float mc) {
-        float mn = fmax_nan(m, mc);
-        float dl = m - mn;  // <= 0, or NaN
-        float s = (dl == 0.f) ? 1.f : ex2(dl * kLog2e);
-        float2 s2 = splat(s);
-        float2 z = add2(zb, zs);
-        t = mul2(fma2(splat(dl), z, t), s2);
-        zb = mul2(zb, s2);
-        zs = mul2(zs, s2);
-        float2 g = add2(add2(zb, splat(kSplit)), splat(-kSplit));
-        zs = add2(zs, diff2(zb, g));
-        zb = g;
+        const float mn = fmax_nan(m, mc);
+        const float dl = m - mn;  // <= 0, or NaN
+        const bool moved = !(dl == 0.f);
+        const float s = moved ? ex2(dl * kLog2e) : 1.f;
+        const float2 z = add2(zs, at_max());
+        t = mul2(fma2(splat(dl), z, t), splat(s));
+        if (moved) {
+            zs = mul2(z, splat(s));
+            ms = splat(0.f);
+            np = 0.f;
+        }
         m = mn;
     }
 
-    // Accumulate two logits given as d = x - m.
+    // Accumulate two logits given as d = x - m; the caller adds the logits per lane to np
+    // once per chunk.
     __device__ __forceinline__ void accum_d(float2 d) {
-        float2 tt = mul2(d, splat(kLog2e));
-        float2 e = make_float2(ex2(tt.x), ex2(tt.y));
-        float2 g = add2(add2(e, splat(kSplit)), splat(-kSplit));
-        zb = add2(zb, g);
-        zs = add2(zs, diff2(e, g));
+        const float2 tt = mul2(d, splat(kLog2e));
+        const float2 e = make_float2(ex2(tt.x), ex2(tt.y));
+        const float2 nz = make_float2(not_zero(d.x), not_zero(d.y));
+        zs = fma2(e, nz, zs);
+        ms = add2(ms, nz);
         t = fma2(e, d, t);
     }
 
     // Accumulate two logits; nm = (-m, -m).
     __device__ __forceinline__ void accum(float2 x, float2 nm) { accum_d(add2(x, nm)); }
 
+    // Z of this thread in fp64 (count at the maximum + the rest).
+    __device__ __forceinline__ double z64() const {
+        const float2 c = at_max();
+        return ((double)c.x + (double)c.y) + ((double)zs.x + (double)zs.y);
+    }
+    __device__ __forceinline__ double t64() const { return (double)t.x + (double)t.y; }
+
     // true when a -inf logit met the fast (unclamped) path: e = 0 times d = -inf made t
     // NaN while z stayed finite.  NaN logits poison z as well and are not flagged.
     __device__ __forceinline__ bool saw_neg_inf() const {
-        return isnan(t.x + t.y) && !isnan(zb.x + zb.y + zs.x + zs.y) && !isnan(m);
+        return isnan(t.x + t.y) && !isnan(zs.x + zs.y) && !isnan(m);
     }
 };
 

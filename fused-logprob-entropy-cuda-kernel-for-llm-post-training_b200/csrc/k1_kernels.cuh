@@ -76,28 +76,32 @@ __device__ __forceinline__ int64_t block_of(int64_t u, int64_t total, int64_t G)
 #ifndef K1_BWD_MINB
 #define K1_BWD_MINB 4
 #endif
-#ifndef K1_PREFETCH
-#define K1_PREFETCH 0
-#endif
 #ifndef K1_MIXED_ADD
-#define K1_MIXED_ADD 0
+#define K1_MIXED_ADD 1
+#endif
+#ifndef K1_FWD_PREFETCH
+#define K1_FWD_PREFETCH 0
 #endif
 
-// CLAMP = false is the fast path: logits are used as loaded.  A -inf logit then turns t
+// clamp = false is the fast path: logits are used as loaded.  A -inf logit then turns t
 // into NaN (0 * -inf), which the caller detects after the segment and re-streams the
-// segment with CLAMP = true, where every logit is first clamped to the lowest finite
-// value of its type.
-template <typename T, int U, bool CLAMP>
-__device__ __forceinline__ void fwd_chunk(const uint4 (&v)[U], FwdState& st) {
+// segment with clamp = true (a block-uniform flag), where every logit is first clamped
+// to the lowest finite value of its type.
+template <typename T, int U>
+__device__ __forceinline__ void fwd_chunk(const uint4 (&v)[U], FwdState& st, bool clamp) {
     using D = DT<T>;
     if constexpr (sizeof(T) == 2) {
         uint32_t w[4 * U];
 #pragma unroll
         for (int u = 0; u < U; ++u) {
-            w[4 * u + 0] = CLAMP ? D::clamp2(v[u].x) : v[u].x;
-            w[4 * u + 1] = CLAMP ? D::clamp2(v[u].y) : v[u].y;
-            w[4 * u + 2] = CLAMP ? D::clamp2(v[u].z) : v[u].z;
-            w[4 * u + 3] = CLAMP ? D::clamp2(v[u].w) : v[u].w;
+            w[4 * u + 0] = v[u].x;
+            w[4 * u + 1] = v[u].y;
+            w[4 * u + 2] = v[u].z;
+            w[4 * u + 3] = v[u].w;
+        }
+        if (clamp) {
+#pragma unroll
+            for (int i = 0; i < 4 * U; ++i) w[i] = D::clamp2(w[i]);
         }
         uint32_t mx[4 * U];
 #pragma unroll
@@ -118,14 +122,19 @@ __device__ __forceinline__ void fwd_chunk(const uint4 (&v)[U], FwdState& st) {
                 st.accum(D::to_f2(w[i]), nm);
             }
         }
+        st.np += (float)(4 * U);
     } else {
         float f[4 * U];
 #pragma unroll
         for (int u = 0; u < U; ++u) {
-            f[4 * u + 0] = CLAMP ? D::clamp1(__uint_as_float(v[u].x)) : __uint_as_float(v[u].x);
-            f[4 * u + 1] = CLAMP ? D::clamp1(__uint_as_float(v[u].y)) : __uint_as_float(v[u].y);
-            f[4 * u + 2] = CLAMP ? D::clamp1(__uint_as_float(v[u].z)) : __uint_as_float(v[u].z);
-            f[4 * u + 3] = CLAMP ? D::clamp1(__uint_as_float(v[u].w)) : __uint_as_float(v[u].w);
+            f[4 * u + 0] = __uint_as_float(v[u].x);
+            f[4 * u + 1] = __uint_as_float(v[u].y);
+            f[4 * u + 2] = __uint_as_float(v[u].z);
+            f[4 * u + 3] = __uint_as_float(v[u].w);
+        }
+        if (clamp) {
+#pragma unroll
+            for (int i = 0; i < 4 * U; ++i) f[i] = D::clamp1(f[i]);
         }
         float mx[4 * U];
 #pragma unroll
@@ -139,6 +148,7 @@ __device__ __forceinline__ void fwd_chunk(const uint4 (&v)[U], FwdState& st) {
         const float2 nm = splat(-st.m);
 #pragma unroll
         for (int i = 0; i < 2 * U; ++i) st.accum(make_float2(f[2 * i], f[2 * i + 1]), nm);
+        st.np += (float)(2 * U);
     }
 }
 
@@ -148,30 +158,62 @@ __device__ __forceinline__ void load_vectors(uint4 (&v)[U], const uint4* vp, int
     for (int u = 0; u < U; ++u) v[u] = ldg_stream(vp + j + (int64_t)u * THREADS);
 }
 
+// Predicated chunk load: vectors at or beyond j1 read as padding (the dtype's lowest
+// finite value, which adds exp(-huge) = 0 and is counted like any sub-maximum logit).
+template <typename T, int U, int THREADS>
+__device__ __forceinline__ void load_vectors_masked(uint4 (&v)[U], const uint4* vp, int64_t j,
+                                                    int64_t j1) {
+    const uint32_t pw = DT<T>::kPadWord;
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+        const int64_t jj = j + (int64_t)u * THREADS;
+        v[u] = (jj < j1) ? ldg_stream(vp + jj) : make_uint4(pw, pw, pw, pw);
+    }
+}
+
+// The remainder of a segment (fewer than U vectors left for this thread): all its loads
+// are issued at once, then reduced two vectors at a time, so it costs one memory round
+// trip and no arithmetic on padding beyond one vector.
+template <typename T, int THREADS, int U>
+__device__ __forceinline__ void fwd_remainder(const uint4* vp, int64_t j, int64_t j1,
+                                              FwdState& st, bool clamp) {
+    uint4 v[U];
+    load_vectors_masked<T, U, THREADS>(v, vp, j, j1);
+#pragma unroll
+    for (int u = 0; u < U; u += 2) {
+        if (j + (int64_t)u * THREADS < j1) {
+            uint4 w[2] = {v[u], v[u + 1]};
+            fwd_chunk<T, 2>(w, st, clamp);
+        }
+    }
+}
+
 // Stream vectors [j0, j1) of one row (vector path: row start 16-byte aligned and the
 // row an exact number of vectors).  `tid` / THREADS: this thread's lane in the group
-// that shares the segment.  With K1_PREFETCH the next chunk's loads are issued before
-// the current chunk is reduced (two register buffers, used alternately).
-template <typename T, int THREADS, int U, bool CLAMP>
+// that shares the segment.  With K1_FWD_PREFETCH the next chunk's loads are in flight
+// while the current chunk is reduced (two register buffers used alternately): warps that
+// start in lock-step (every warp of the grid issues its first loads together) would
+// otherwise alternate between waiting for memory and computing instead of overlapping.
+template <typename T, int THREADS, int U>
 __device__ __forceinline__ void fwd_stream_vec(const T* rowp, int64_t j0, int64_t j1,
-                                               FwdState& st, int tid) {
+                                               FwdState& st, int tid, bool clamp) {
     const uint4* vp = reinterpret_cast<const uint4*>(rowp);
     constexpr int64_t kSpan = (int64_t)(U - 1) * THREADS;
     constexpr int64_t kStep = (int64_t)U * THREADS;
     int64_t j = j0 + tid;
-    if constexpr (K1_PREFETCH) {
+    if constexpr (K1_FWD_PREFETCH) {
         if (j + kSpan < j1) {
             uint4 a[U], b[U];
             load_vectors<U, THREADS>(a, vp, j);
             while (true) {
                 bool more = j + kStep + kSpan < j1;
                 if (more) load_vectors<U, THREADS>(b, vp, j + kStep);
-                fwd_chunk<T, U, CLAMP>(a, st);
+                fwd_chunk<T, U>(a, st, clamp);
                 j += kStep;
                 if (!more) break;
                 more = j + kStep + kSpan < j1;
                 if (more) load_vectors<U, THREADS>(a, vp, j + kStep);
-                fwd_chunk<T, U, CLAMP>(b, st);
+                fwd_chunk<T, U>(b, st, clamp);
                 j += kStep;
                 if (!more) break;
             }
@@ -180,14 +222,10 @@ __device__ __forceinline__ void fwd_stream_vec(const T* rowp, int64_t j0, int64_
         for (; j + kSpan < j1; j += kStep) {
             uint4 v[U];
             load_vectors<U, THREADS>(v, vp, j);
-            fwd_chunk<T, U, CLAMP>(v, st);
+            fwd_chunk<T, U>(v, st, clamp);
         }
     }
-    for (; j < j1; j += THREADS) {
-        uint4 v[1];
-        v[0] = ldg_stream(vp + j);
-        fwd_chunk<T, 1, CLAMP>(v, st);
-    }
+    if (j < j1) fwd_remainder<T, THREADS, U>(vp, j, j1, st, clamp);
 }
 
 // Stream elements [j0, j1) of one row (scalar path: any alignment).
@@ -210,6 +248,7 @@ __device__ __forceinline__ void fwd_stream_scalar(const T* rowp, int64_t j0, int
         const float2 nm = splat(-st.m);
 #pragma unroll
         for (int i = 0; i < U / 2; ++i) st.accum(make_float2(f[2 * i], f[2 * i + 1]), nm);
+        st.np += (float)(U / 2);
     }
 }
 
@@ -372,26 +411,21 @@ __global__ void __launch_bounds__(THREADS, K1_FWD_MINB) k1_fwd_kernel(FwdParams 
         const int64_t j1 = min(p.vpr, j0 + (end - start));
         const T* rowp = reinterpret_cast<const T*>(p.logits) + p.lay.offset(r);
         FwdState st;
-        st.init();
         RowPartial part;
         if constexpr (VEC) {
-            fwd_stream_vec<T, THREADS, U, false>(rowp, j0, j1, st, tid);
-            const double z = ((double)st.zb.x + (double)st.zb.y) + ((double)st.zs.x + (double)st.zs.y);
-            const double t = (double)st.t.x + (double)st.t.y;
-            if (!seg_merge<THREADS, BAR>(st.m, z, t, st.m <= DT<T>::kLowest, st.saw_neg_inf(), sm,
-                                         buf, part)) {
-                // rare: the segment holds -inf logits; stream it again, clamped
+            // second pass only when the segment holds -inf logits: stream it again, clamped
+            for (int pass = 0; pass < 2; ++pass) {
                 st.init();
-                fwd_stream_vec<T, THREADS, U, true>(rowp, j0, j1, st, tid);
-                const double z2 = ((double)st.zb.x + (double)st.zb.y) + ((double)st.zs.x + (double)st.zs.y);
-                const double t2 = (double)st.t.x + (double)st.t.y;
-                seg_merge<THREADS, BAR>(st.m, z2, t2, st.m <= DT<T>::kLowest, false, sm, buf, part);
+                fwd_stream_vec<T, THREADS, U>(rowp, j0, j1, st, tid, pass == 1);
+                if (seg_merge<THREADS, BAR>(st.m, st.z64(), st.t64(), st.m <= DT<T>::kLowest,
+                                            pass == 0 && st.saw_neg_inf(), sm, buf, part))
+                    break;
             }
         } else {
+            st.init();
             fwd_stream_scalar<T, THREADS>(rowp, j0, j1, st);
-            const double z = ((double)st.zb.x + (double)st.zb.y) + ((double)st.zs.x + (double)st.zs.y);
-            const double t = (double)st.t.x + (double)st.t.y;
-            seg_merge<THREADS, BAR>(st.m, z, t, st.m <= DT<T>::kLowest, false, sm, buf, part);
+            seg_merge<THREADS, BAR>(st.m, st.z64(), st.t64(), st.m <= DT<T>::kLowest, false, sm,
+                                    buf, part);
         }
         buf ^= 1;
         if (j0 == 0 && j1 == p.vpr) {
@@ -557,36 +591,25 @@ __global__ void __launch_bounds__(THREADS, K1_BWD_MINB) k1_bwd_kernel(BwdParams 
                     stg_stream(dv + jj, o);
                 }
             };
-            if constexpr (K1_PREFETCH) {
-                if (j + kSpan < j1) {
-                    uint4 a[U], b[U];
-                    load_vectors<U, THREADS>(a, xv, j);
-                    while (true) {
-                        bool more = j + kStep + kSpan < j1;
-                        if (more) load_vectors<U, THREADS>(b, xv, j + kStep);
-                        emit(a, j);
-                        j += kStep;
-                        if (!more) break;
-                        more = j + kStep + kSpan < j1;
-                        if (more) load_vectors<U, THREADS>(a, xv, j + kStep);
-                        emit(b, j);
-                        j += kStep;
-                        if (!more) break;
+            for (; j + kSpan < j1; j += kStep) {
+                uint4 v[U];
+                load_vectors<U, THREADS>(v, xv, j);
+                emit(v, j);
+            }
+            if (j < j1) {  // remainder: one predicated chunk
+                uint4 v[U];
+                load_vectors_masked<T, U, THREADS>(v, xv, j, j1);
+#pragma unroll
+                for (int u = 0; u < U; ++u) {
+                    const int64_t jj = j + (int64_t)u * THREADS;
+                    if (jj < j1) {
+                        uint4 o = bwd_vector<T>(v[u], q);
+                        const uint64_t k = (uint64_t)(q.tl - jj * EPV);
+                        if (k < (uint64_t)EPV)
+                            o = vec_set<T>(o, (int)k, bwd_target_value(D::load1(xr + q.tl), q));
+                        stg_stream(dv + jj, o);
                     }
                 }
-            } else {
-                for (; j + kSpan < j1; j += kStep) {
-                    uint4 v[U];
-                    load_vectors<U, THREADS>(v, xv, j);
-                    emit(v, j);
-                }
-            }
-            for (; j < j1; j += THREADS) {
-                uint4 o = bwd_vector<T>(ldg_stream(xv + j), q);
-                const uint64_t k = (uint64_t)(q.tl - j * EPV);
-                if (k < (uint64_t)EPV)
-                    o = vec_set<T>(o, (int)k, bwd_target_value(D::load1(xr + q.tl), q));
-                stg_stream(dv + j, o);
             }
         } else {
             for (int64_t j = j0 + threadIdx.x; j < j1; j += THREADS) {

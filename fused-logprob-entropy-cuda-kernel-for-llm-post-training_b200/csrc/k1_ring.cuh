@@ -1,9 +1,9 @@
-// k1_ring.cuh -- bulk-copy (TMA) ring variant of the backward kernel.
+// k1_ring.cuh -- bulk-copy (TMA) ring variants of the forward and backward kernels.
 //
 // One producer warp per block streams the block's rows in chunks of up to SBYTES with
 // cp.async.bulk (global -> shared, completion counted on an mbarrier) into a ring of
-// STAGES buffers; NCW consumer warps transform and store straight out of shared memory,
-// then release the buffer on a second mbarrier.  The
+// STAGES buffers; NCW consumer warps reduce (forward) or transform and store (backward)
+// straight out of shared memory, then release the buffer on a second mbarrier.  The
 // number of bytes in flight per SM is set by the ring size, not by registers.
 //
 // Every mbarrier wait is bounded (kMaxTries polls with a suspend hint, a few seconds in
@@ -17,7 +17,10 @@
 #include "k1_kernels.cuh"
 
 #ifndef K1_RING_MINB
-#define K1_RING_MINB 1
+#define K1_RING_MINB 2
+#endif
+#ifndef K1_RING_FWD_MINB
+#define K1_RING_FWD_MINB 2
 #endif
 
 namespace k1 {
@@ -124,6 +127,111 @@ __device__ __forceinline__ void produce(const void* base, const RowLayout& lay, 
 }
 
 }  // namespace ring
+
+template <typename T, int NCW, int STAGES, int SBYTES, bool SHARD>
+__global__ void __launch_bounds__((NCW + 1) * 32, K1_RING_FWD_MINB) k1_fwd_ring_kernel(FwdParams p) {
+    constexpr int NC = NCW * 32;
+    constexpr int BAR = 1;  // named barrier of the consumer warps (the producer returns early)
+    constexpr int SV = SBYTES / 16;
+    constexpr int VPT = SV / NC;
+    static_assert(SV % NC == 0, "stage must hold a whole number of vectors per consumer");
+    extern __shared__ __align__(128) uint4 ring_buf[];
+    __shared__ __align__(8) uint64_t full[STAGES];
+    __shared__ __align__(8) uint64_t empty[STAGES];
+    __shared__ FwdSmem<NC> sm;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; ++s) {
+            ring::bar_init(&full[s], 1);
+            ring::bar_init(&empty[s], NCW);
+        }
+        ring::fence_init();
+    }
+    __syncthreads();
+    const int64_t G = gridDim.x, b = blockIdx.x;
+    const int64_t start = b * p.total / G, end = (b + 1) * p.total / G;
+    if (warp == NCW) {
+        if (lane == 0)
+            ring::produce<STAGES, SV>(p.logits, p.lay, (int)sizeof(T), p.vpr, start, end, ring_buf,
+                                      full, empty);
+        return;
+    }
+    const int tid = threadIdx.x;
+    const uint32_t pw = DT<T>::kPadWord;
+    ring::ChunkWalk w;
+    w.begin(start, end, p.vpr);
+    const int64_t first_row = w.r;
+    int64_t split_row[2] = {-1, -1};
+    unsigned split_prev[2] = {0u, 0u};
+    int count = 0, buf = 0;
+    uint32_t k = 0;
+    bool ok = true;
+    while (w.pos < w.end) {
+        const int64_t r = w.r, j0 = w.j0, j1 = w.j1;
+        const T* rowp = reinterpret_cast<const T*>(p.logits) + p.lay.offset(r);
+        FwdState st;
+        st.init();
+        for (int64_t jj = j0; jj < j1; jj += SV) {
+            const int64_t n = min((int64_t)SV, j1 - jj);
+            const uint32_t s = k % STAGES, use = k / STAGES;
+            if (ok) ok = ring::wait(&full[s], use & 1);
+            const uint4* stage = ring_buf + (size_t)s * SV;
+            if (ok) {
+                uint4 v[VPT];
+#pragma unroll
+                for (int u = 0; u < VPT; ++u)
+                    v[u] = (tid + u * NC < n) ? stage[tid + u * NC] : make_uint4(pw, pw, pw, pw);
+                fwd_chunk<T, VPT>(v, st, false);
+            }
+            __syncwarp();
+            if (lane == 0) ring::arrive(&empty[s]);
+            ++k;
+        }
+        RowPartial part;
+        if (!seg_merge<NC, BAR>(st.m, st.z64(), st.t64(), st.m <= DT<T>::kLowest,
+                                st.saw_neg_inf(), sm, buf, part)) {
+            // rare: the segment holds -inf logits; stream it again from global, clamped
+            st.init();
+            fwd_stream_vec<T, NC, 4>(rowp, j0, j1, st, tid, true);
+            seg_merge<NC, BAR>(st.m, st.z64(), st.t64(), st.m <= DT<T>::kLowest, false, sm, buf,
+                               part);
+        }
+        buf ^= 1;
+        if (j0 == 0 && j1 == p.vpr) {
+            if (tid == 0) {
+                sm.done_row[count] = r;
+                sm.done_part[count] = part;
+            }
+            if (++count == kRowCap) {
+                fwd_flush_rows<T, NC, BAR, SHARD>(p, sm, count);
+                count = 0;
+            }
+        } else {
+            const int slot = (r == first_row) ? 0 : 1;
+            split_row[slot] = r;
+            if (tid == 0) {
+                p.ws_part[2 * b + slot] = part;
+                __threadfence();
+                split_prev[slot] = atomicAdd(p.ws_ticket + block_of(r * p.vpr, p.total, G), 1u);
+            }
+        }
+        w.next_row(p.vpr);
+    }
+    if (tid == 0) {
+        sm.split_prev[0] = split_prev[0];
+        sm.split_prev[1] = split_prev[1];
+    }
+    fwd_flush_rows<T, NC, BAR, SHARD>(p, sm, count);
+#pragma unroll
+    for (int slot = 0; slot < 2; ++slot) {
+        const int64_t sr = split_row[slot];
+        if (sr < 0) continue;
+        const int64_t bf = block_of(sr * p.vpr, p.total, G);
+        const int64_t bl = block_of((sr + 1) * p.vpr - 1, p.total, G);
+        if (sm.split_prev[slot] == (unsigned)(bl - bf))
+            fwd_merge_split_row<T, NC, BAR, SHARD>(p, sr, sm.merge);
+    }
+}
 
 template <typename T, int NCW, int STAGES, int SBYTES>
 __global__ void __launch_bounds__((NCW + 1) * 32, K1_RING_MINB) k1_bwd_ring_kernel(BwdParams p) {

@@ -327,4 +327,12 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
     m.def("vocab_combine", &vocab_combine, "Vocab-parallel: merge gathered shard partials.");
     m.def("vocab_shard_backward", &vocab_shard_backward, "Vocab-parallel: backward of a shard.");
     m.def("abi_version", &k1_abi_version, "C ABI version of the loaded libk1_b200.so.");
+    m.def(
+        "ring_status",
+        []() {
+            unsigned v = 0;
+            check_rc(k1_ring_status(&v));
+            return v;
+        },
+        "Read and clear the bulk-copy ring's timeout word of the current device (0 = ok).");
 }

@@ -1,0 +1,133 @@
+"""K1 forward + backward for logits that live in host memory.
+
+`fused_logprob_entropy_fwd_bwd_host` streams the rows through the GPU in chunks: while
+chunk i is reduced and differentiated on the device, chunk i+1 is copied in and chunk
+i-1's gradient is copied out, on three CUDA streams with events between them.  The
+transfer in and the transfer out then overlap, so a step costs about one direction of
+the host link instead of both.  Use it when the [N, V] logits (and their gradient) are
+kept in host memory, e.g. offloaded activations; with device-resident logits call
+`kernel_opt.fused_logprob_entropy` instead.
+
+The upstream gradients are per row and known before the call (as for a policy-gradient
+loss whose per-token weights come from advantages and masks), so each chunk's backward
+can run right after its forward.  Rows are independent, so chunking changes no result.
+"""
+from __future__ import annotations
+
+import torch
+
+from kernel_opt import _C
+
+
+_STREAMS: dict = {}
+
+
+def _streams(dev: torch.device):
+    # three persistent side streams per device (copy in, compute, copy out)
+    if dev not in _STREAMS:
+        _STREAMS[dev] = tuple(torch.cuda.Stream(dev) for _ in range(3))
+    return _STREAMS[dev]
+
+
+def _rows2d(t: torch.Tensor, V: int) -> torch.Tensor:
+    if not t.is_contiguous():
+        raise ValueError("host logits / gradient buffers must be contiguous")
+    return t.view(-1, V)
+
+
+def fused_logprob_entropy_fwd_bwd_host(logits: torch.Tensor, targets: torch.Tensor,
+                                       g_logp: torch.Tensor | None = None,
+                                       g_ent: torch.Tensor | None = None,
+                                       g_lse: torch.Tensor | None = None,
+                                       d_logits: torch.Tensor | None = None,
+                                       outputs: tuple | None = None,
+                                       chunk_rows: int | None = None,
+                                       device: torch.device | int | None = None):
+    """Forward and backward of K1 over host-resident logits.
+
+    Args:
+        logits:  CPU tensor [..., V] (bf16 / fp16 / fp32), contiguous; pinned memory is
+                 needed for the copies to overlap.
+        targets: [...] int64 (CPU or CUDA).
+        g_logp, g_ent, g_lse: upstream gradients [...] (fp32, CPU or CUDA) or None (zero).
+        d_logits: CPU tensor like `logits` for the gradient (allocated pinned if None);
+                 may be `logits` itself, which is then overwritten chunk by chunk.
+        outputs: optional (logprob, entropy, lse) CPU fp32 tensors shaped like targets.
+        chunk_rows: rows per chunk (default: about 32 MB of logits per chunk).
+        device: CUDA device (default: current).
+
+    Returns (logprob, entropy, lse, d_logits) on the host.  The call returns when all
+    host buffers hold their results.
+    """
+    dev = torch.device("cuda", torch.cuda.current_device() if device is None else
+                       (device.index if isinstance(device, torch.device) else device))
+    if logits.is_cuda:
+        raise ValueError("logits must be in host memory (use fused_logprob_entropy on device)")
+    V = logits.shape[-1]
+    x = _rows2d(logits, V)
+    N = x.shape[0]
+    if targets.numel() != N:
+        raise ValueError("targets numel must match leading dims of logits")
+    if d_logits is None:
+        d_logits = torch.empty_like(logits, pin_memory=True)
+    d = _rows2d(d_logits, V)
+    if outputs is None:
+        outputs = tuple(torch.empty(targets.shape, dtype=torch.float32, pin_memory=True)
+                        for _ in range(3))
+    outs = [o.view(-1) for o in outputs]
+    if N == 0:
+        return (*outputs, d_logits)
+
+    esize = x.element_size()
+    if chunk_rows is None:
+        chunk_rows = max(1, (32 << 20) // (V * esize))
+    R = min(chunk_rows, N)
+    nchunks = (N + R - 1) // R
+
+    # small per-row inputs go to the device once
+    t_dev = targets.reshape(-1).to(dev, non_blocking=True)
+    grads = [None if g is None else g.reshape(-1).to(dev, torch.float32, non_blocking=True)
+             for g in (g_logp, g_ent, g_lse)]
+    o_dev = [torch.empty(N, dtype=torch.float32, device=dev) for _ in range(3)]
+
+    main = torch.cuda.current_stream(dev)
+    s_in, s_run, s_out = _streams(dev)
+    nbuf = 3
+    bufs = [torch.empty((R, V), dtype=x.dtype, device=dev) for _ in range(min(nbuf, nchunks))]
+    ev_in = [torch.cuda.Event() for _ in bufs]
+    ev_run = [torch.cuda.Event() for _ in bufs]
+    ev_out = [torch.cuda.Event() for _ in bufs]
+    start = torch.cuda.Event()
+    start.record(main)
+    for s in (s_in, s_run, s_out):
+        s.wait_event(start)
+
+    for i in range(nchunks):
+        a, b = i * R, min(N, (i + 1) * R)
+        k = i % len(bufs)
+        buf = bufs[k][: b - a]
+        with torch.cuda.stream(s_in):
+            if i >= len(bufs):
+                s_in.wait_event(ev_out[k])  # the buffer's previous gradient has left
+            buf.copy_(x[a:b], non_blocking=True)
+            ev_in[k].record(s_in)
+        with torch.cuda.stream(s_run):
+            s_run.wait_event(ev_in[k])
+            lp, h, l = (o[a:b] for o in o_dev)
+            tt = t_dev[a:b]
+            _C.fused_logprob_entropy_v1(buf, tt, lp, h, l)
+            gg = [None if g is None else g[a:b] for g in grads]
+            _C.fused_logprob_entropy_v1_backward(buf, tt, l, h, *gg, buf)  # in place
+            ev_run[k].record(s_run)
+        with torch.cuda.stream(s_out):
+            s_out.wait_event(ev_run[k])
+            d[a:b].copy_(buf, non_blocking=True)
+            ev_out[k].record(s_out)
+
+    with torch.cuda.stream(s_out):
+        s_out.wait_stream(s_run)
+        for o, od in zip(outs, o_dev):
+            o.copy_(od, non_blocking=True)
+    main.wait_stream(s_out)
+    main.synchronize()  # host buffers hold the results; device buffers are free again
+    return (*outputs, d_logits)

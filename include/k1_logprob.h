@@ -5,8 +5,9 @@
  *
  * Every entry point takes plain device pointers, element counts/strides and a CUDA
  * stream handle (cudaStream_t passed as void*; NULL = legacy default stream).  No
- * entry point allocates device memory, synchronises the stream, or keeps state
- * between calls other than a cached per-device SM count.  The caller owns every
+ * entry point allocates device memory; only the k1_ring_status diagnostic synchronises;
+ * state kept between calls is limited to cached per-device launch parameters (SM count,
+ * resident blocks per kernel) and the ring's timeout word.  The caller owns every
  * output buffer, exactly like the reference's torch binding, whose host functions
  * only write into out-parameters (reference: csrc/fused_logprob.cu:284-458,
  * python/kernel_opt/ops.py:24-30,83).
@@ -77,6 +78,14 @@ const char* k1_last_error(void);
 
 /* K1_ABI_VERSION of the loaded library. */
 int k1_abi_version(void);
+
+/*
+ * Diagnostic: the kernels that stream through a shared-memory ring of bulk copies bound
+ * every wait on the ring's barriers; a wait that runs out sets a per-device word instead
+ * of hanging.  This reads and clears that word for the current device (*out = 0: no wait
+ * ran out).  Synchronises with the device.  No counterpart in the reference.
+ */
+int k1_ring_status(unsigned* out);
 
 /*
  * Device scratch needed by k1_fused_logprob_entropy_v1 and k1_vocab_shard_partials

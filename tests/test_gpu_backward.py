@@ -152,3 +152,12 @@ def test_backward_ragged_and_split(dtype):
         g = grads_like((n,), seed=V)
         d = autograd_grad(x, t, g)
         check_grad(d, x, t, *g, what=f"{dtype} {n}x{V}")
+
+
+def test_no_ring_wait_ran_out():
+    """The bulk-copy ring bounds every barrier wait; none may have run out in this run."""
+    x = seeded_logits((64, 32000), torch.bfloat16, 3.0, seed=60)
+    t = seeded_targets((64,), 32000)
+    autograd_grad(x, t, grads_like((64,), seed=61))
+    torch.cuda.synchronize()
+    assert _C.ring_status() == 0
