@@ -30,6 +30,29 @@ int fail(int code, const char* fmt, ...) {
     return code;
 }
 
+#ifndef K1_PDL
+#define K1_PDL 1
+#endif
+
+// Launch with programmatic stream serialization (see pdl_wait / pdl_trigger): the grid
+// may be scheduled while the previous kernel of the stream drains; it waits for that
+// kernel's completion on the device before touching memory.
+template <typename... KArgs, typename... Args>
+cudaError_t launch(void (*kernel)(KArgs...), int64_t grid, int block, size_t smem,
+                   cudaStream_t stream, Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)grid);
+    cfg.blockDim = dim3((unsigned)block);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = K1_PDL ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, kernel, args...);
+}
+
 int check_launch(const char* what) {
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess)
@@ -37,7 +60,11 @@ int check_launch(const char* what) {
     return K1_OK;
 }
 
-constexpr int kThreads = 256;
+#ifndef K1_FWD_THREADS
+#define K1_FWD_THREADS 256
+#endif
+constexpr int kThreads = 256;                  // backward (register path), naive helpers
+constexpr int kFwdThreads = K1_FWD_THREADS;    // forward block size
 constexpr int kUnroll = K1_FWD_UNROLL;      // 16-byte vectors per thread and chunk (forward)
 constexpr int kUnrollBwd = K1_BWD_UNROLL;   // 16-byte vectors per thread and chunk (backward)
 #ifndef K1_RING
@@ -47,7 +74,7 @@ constexpr int kUnrollBwd = K1_BWD_UNROLL;   // 16-byte vectors per thread and ch
 #define K1_RING_FWD 0
 #endif
 #ifndef K1_RING_WARPS
-#define K1_RING_WARPS 8
+#define K1_RING_WARPS 16
 #endif
 #ifndef K1_RING_STAGES
 #define K1_RING_STAGES 4
@@ -219,17 +246,17 @@ int launch_forward(const char* fn, const void* logits, const Rows& L, int64_t co
         const size_t smem = (size_t)kRingStages * kRingBytes;
         rc = grid_for(kern, dev, p.total, kMinUnitsPerBlockVec, &grid, threads, smem);
         if (rc) return rc;
-        kern<<<(unsigned)grid, threads, smem, stream>>>(p);
+        launch(kern, grid, threads, smem, stream, p);
     } else if (vec) {
-        auto kern = k1::k1_fwd_kernel<T, kThreads, kUnroll, true, SHARD>;
-        rc = grid_for(kern, dev, p.total, kMinUnitsPerBlockVec, &grid);
+        auto kern = k1::k1_fwd_kernel<T, kFwdThreads, kUnroll, true, SHARD>;
+        rc = grid_for(kern, dev, p.total, kMinUnitsPerBlockVec, &grid, kFwdThreads);
         if (rc) return rc;
-        kern<<<(unsigned)grid, kThreads, 0, stream>>>(p);
+        launch(kern, grid, kFwdThreads, 0, stream, p);
     } else {
-        auto kern = k1::k1_fwd_kernel<T, kThreads, kUnroll, false, SHARD>;
-        rc = grid_for(kern, dev, p.total, kMinUnitsPerBlockScalar, &grid);
+        auto kern = k1::k1_fwd_kernel<T, kFwdThreads, kUnroll, false, SHARD>;
+        rc = grid_for(kern, dev, p.total, kMinUnitsPerBlockScalar, &grid, kFwdThreads);
         if (rc) return rc;
-        kern<<<(unsigned)grid, kThreads, 0, stream>>>(p);
+        launch(kern, grid, kFwdThreads, 0, stream, p);
     }
     return check_launch(fn);
 }
@@ -267,17 +294,17 @@ int launch_backward(const char* fn, const void* logits, const Rows& L, const Row
         const size_t smem = (size_t)kRingStages * kRingBytes;
         rc = grid_for(kern, dev, p.total, kMinUnitsPerBlockVec, &grid, threads, smem);
         if (rc) return rc;
-        kern<<<(unsigned)grid, threads, smem, stream>>>(p);
+        launch(kern, grid, threads, smem, stream, p);
     } else if (vec) {
         auto kern = k1::k1_bwd_kernel<T, kThreads, kUnrollBwd, true>;
         rc = grid_for(kern, dev, p.total, kMinUnitsPerBlockVec, &grid);
         if (rc) return rc;
-        kern<<<(unsigned)grid, kThreads, 0, stream>>>(p);
+        launch(kern, grid, kThreads, 0, stream, p);
     } else {
         auto kern = k1::k1_bwd_kernel<T, kThreads, kUnrollBwd, false>;
         rc = grid_for(kern, dev, p.total, kMinUnitsPerBlockScalar, &grid);
         if (rc) return rc;
-        kern<<<(unsigned)grid, kThreads, 0, stream>>>(p);
+        launch(kern, grid, kThreads, 0, stream, p);
     }
     return check_launch(fn);
 }
@@ -366,19 +393,19 @@ int k1_fused_logprob_entropy_naive(const void* logits, int dtype, int64_t n_rows
     k1::RowLayout lay = layout_of(L);
     switch (dtype) {
         case K1_DTYPE_BF16:
-            k1::k1_naive_kernel<__nv_bfloat16><<<(unsigned)blocks, threads, 0, s>>>(
-                reinterpret_cast<const __nv_bfloat16*>(logits), n_rows, vocab, lay, targets,
-                logprob, entropy, lse);
+            launch(k1::k1_naive_kernel<__nv_bfloat16>, blocks, threads, 0, s,
+                   reinterpret_cast<const __nv_bfloat16*>(logits), n_rows, vocab, lay, targets,
+                   logprob, entropy, lse);
             break;
         case K1_DTYPE_F16:
-            k1::k1_naive_kernel<__half><<<(unsigned)blocks, threads, 0, s>>>(
-                reinterpret_cast<const __half*>(logits), n_rows, vocab, lay, targets, logprob,
-                entropy, lse);
+            launch(k1::k1_naive_kernel<__half>, blocks, threads, 0, s,
+                   reinterpret_cast<const __half*>(logits), n_rows, vocab, lay, targets, logprob,
+                   entropy, lse);
             break;
         default:
-            k1::k1_naive_kernel<float><<<(unsigned)blocks, threads, 0, s>>>(
-                reinterpret_cast<const float*>(logits), n_rows, vocab, lay, targets, logprob,
-                entropy, lse);
+            launch(k1::k1_naive_kernel<float>, blocks, threads, 0, s,
+                   reinterpret_cast<const float*>(logits), n_rows, vocab, lay, targets, logprob,
+                   entropy, lse);
             break;
     }
     return check_launch(fn);
@@ -466,8 +493,8 @@ int k1_vocab_combine(const k1_partial* gathered, int n_shards, int64_t n_rows, f
     cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
     const int threads = 128;
     const int64_t blocks = (n_rows + threads - 1) / threads;
-    k1::k1_vocab_combine_kernel<<<(unsigned)blocks, threads, 0, s>>>(gathered, n_shards, n_rows,
-                                                                     logprob, entropy, lse);
+    launch(k1::k1_vocab_combine_kernel, blocks, threads, 0, s, gathered, n_shards, n_rows,
+           logprob, entropy, lse);
     return check_launch(fn);
 }
 

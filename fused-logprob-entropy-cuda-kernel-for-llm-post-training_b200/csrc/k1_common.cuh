@@ -44,6 +44,17 @@ __device__ __forceinline__ float not_zero(float d) {
     return y;
 }
 
+// Programmatic dependent launch.  Every K1 kernel is launched so that it may start
+// before the previous kernel in the stream has finished; pdl_wait() then blocks until
+// that kernel has completed and its writes are visible, and must come before the first
+// global-memory access.  pdl_trigger() lets the next kernel in the stream be scheduled
+// into the slots this grid frees as its blocks finish.  Both are no-ops for launches
+// without the attribute.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // NaN-propagating max (fmaxf drops NaN; the reference's outputs become NaN when a
 // row holds one, and so do ours).
 __device__ __forceinline__ float fmax_nan(float a, float b) {

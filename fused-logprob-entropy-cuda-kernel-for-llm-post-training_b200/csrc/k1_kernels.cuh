@@ -286,7 +286,6 @@ struct FwdSmem {
     int wbad[2][NW];     // per-warp "saw -inf on the fast path"
     double wz[2][NW];
     double wt[2][NW];
-    ReduceSmem<THREADS> merge;  // split-row merges at the end of the block
     RowPartial done_part[kRowCap];
     int64_t done_row[kRowCap];
     unsigned split_prev[2];  // ticket values of the block's first / last split row
@@ -360,21 +359,31 @@ __device__ __forceinline__ void fwd_flush_rows(const FwdParams& p, FwdSmem<THREA
 }
 
 // Split row r (its vectors span blocks bf..bl): merge every block's published piece and
-// write the row.  Called by the block that drew the last ticket.
-template <typename T, int THREADS, int BAR, bool SHARD>
-__device__ __forceinline__ void fwd_merge_split_row(const FwdParams& p, int64_t r,
-                                                    ReduceSmem<THREADS>& sm) {
-    const int tid = threadIdx.x;
+// write the row.  Called by the block that drew the last ticket, after its own loop; one
+// warp does the work with shuffles (no block barrier), lane 0 issues the target-logit
+// load first so that its latency overlaps the loads of the pieces.
+template <typename T, bool SHARD>
+__device__ __forceinline__ void fwd_merge_split_row(const FwdParams& p, int64_t r) {
+    const int lane = threadIdx.x & 31;
     const int64_t G = gridDim.x;
     const int64_t bf = block_of(r * p.vpr, p.total, G);
     const int64_t bl = block_of((r + 1) * p.vpr - 1, p.total, G);
+    const T* rowp = reinterpret_cast<const T*>(p.logits) + p.lay.offset(r);
+    float xt = 0.f;
+    bool has = false;
+    if (lane == 0) {
+        const int64_t tg = p.targets[r];
+        const int64_t tl = SHARD ? tg - p.col_offset : tg;
+        has = (tg >= 0) && (tl >= 0) && (tl < p.vocab);
+        if (has) xt = DT<T>::load1(rowp + tl);
+    }
     __threadfence();
     RowPartial acc;
     acc.z = 0.0;
     acc.t = 0.0;
     acc.m = -INFINITY;
     acc.pad = 0.f;
-    for (int64_t c = bf + tid; c <= bl; c += THREADS) {
+    for (int64_t c = bf + lane; c <= bl; c += 32) {
         const int64_t fr = (c * p.total / G) / p.vpr;
         const RowPartial* q = p.ws_part + 2 * c + (r == fr ? 0 : 1);
         RowPartial qq;
@@ -384,9 +393,28 @@ __device__ __forceinline__ void fwd_merge_split_row(const FwdParams& p, int64_t 
         qq.pad = 0.f;
         acc = merge_partials(acc, qq);
     }
-    RowPartial tot = block_merge<THREADS, BAR>(acc.m, acc.z, acc.t, acc.m == -INFINITY, sm);
-    if (tid == 0) {
-        fwd_emit_row<T, SHARD>(p, r, reinterpret_cast<const T*>(p.logits) + p.lay.offset(r), tot);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        RowPartial other;
+        other.z = __shfl_xor_sync(0xffffffffu, acc.z, o);
+        other.t = __shfl_xor_sync(0xffffffffu, acc.t, o);
+        other.m = __shfl_xor_sync(0xffffffffu, acc.m, o);
+        other.pad = 0.f;
+        acc = merge_partials(acc, other);
+    }
+    if (lane == 0) {
+        if constexpr (SHARD) {
+            k1_partial out;
+            out.z = acc.z;
+            out.t = acc.t;
+            out.m = acc.m;
+            out.x_t = has ? xt : 0.f;
+            out.has_target = has ? 1 : 0;
+            out.reserved = 0;
+            p.partials[r] = out;
+        } else {
+            finalize_row(acc, has ? (double)xt : 0.0, p.logprob + r, p.entropy + r, p.lse + r);
+        }
         p.ws_ticket[bf] = 0u;  // leave the workspace zeroed for the next call
     }
 }
@@ -395,6 +423,8 @@ template <typename T, int THREADS, int U, bool VEC, bool SHARD>
 __global__ void __launch_bounds__(THREADS, K1_FWD_MINB) k1_fwd_kernel(FwdParams p) {
     constexpr int BAR = 0;
     __shared__ FwdSmem<THREADS> sm;
+    pdl_wait();
+    pdl_trigger();
     const int tid = threadIdx.x;
     const int64_t G = gridDim.x, b = blockIdx.x;
     const int64_t start0 = b * p.total / G;
@@ -458,14 +488,16 @@ __global__ void __launch_bounds__(THREADS, K1_FWD_MINB) k1_fwd_kernel(FwdParams 
         sm.split_prev[1] = split_prev[1];
     }
     fwd_flush_rows<T, THREADS, BAR, SHARD>(p, sm, count);  // its barrier publishes split_prev
-#pragma unroll
-    for (int slot = 0; slot < 2; ++slot) {
-        const int64_t sr = split_row[slot];
-        if (sr < 0) continue;
-        const int64_t bf = block_of(sr * p.vpr, p.total, G);
-        const int64_t bl = block_of((sr + 1) * p.vpr - 1, p.total, G);
-        if (sm.split_prev[slot] == (unsigned)(bl - bf))
-            fwd_merge_split_row<T, THREADS, BAR, SHARD>(p, sr, sm.merge);
+    // split rows this block finishes: the first one by warp 0, the last one by warp 1
+    const int slot = tid >> 5;
+    if (slot < 2) {
+        const int64_t sr = slot == 0 ? split_row[0] : split_row[1];
+        if (sr >= 0) {
+            const int64_t bf = block_of(sr * p.vpr, p.total, G);
+            const int64_t bl = block_of((sr + 1) * p.vpr - 1, p.total, G);
+            const unsigned prev = slot == 0 ? sm.split_prev[0] : sm.split_prev[1];
+            if (prev == (unsigned)(bl - bf)) fwd_merge_split_row<T, SHARD>(p, sr);
+        }
     }
 }
 
@@ -552,6 +584,8 @@ template <typename T, int THREADS, int U, bool VEC>
 __global__ void __launch_bounds__(THREADS, K1_BWD_MINB) k1_bwd_kernel(BwdParams p) {
     using D = DT<T>;
     constexpr int EPV = VEC ? D::kEPV : 1;
+    pdl_wait();
+    pdl_trigger();
     const int64_t G = gridDim.x, b = blockIdx.x;
     int64_t start = b * p.total / G;
     const int64_t end = (b + 1) * p.total / G;
@@ -641,6 +675,8 @@ template <typename T>
 __global__ void k1_naive_kernel(const T* logits, int64_t n_rows, int64_t vocab, RowLayout lay,
                                 const int64_t* targets, float* logprob, float* entropy,
                                 float* lse) {
+    pdl_wait();
+    pdl_trigger();
     const int64_t r = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (r >= n_rows) return;
     const T* row = logits + lay.offset(r);
@@ -683,6 +719,8 @@ __global__ void k1_naive_kernel(const T* logits, int64_t n_rows, int64_t vocab, 
 // ---------------------------------------------------------------------------------
 __global__ void k1_vocab_combine_kernel(const k1_partial* g, int n_shards, int64_t n_rows,
                                         float* logprob, float* entropy, float* lse) {
+    pdl_wait();
+    pdl_trigger();
     const int64_t r = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (r >= n_rows) return;
     RowPartial acc;

@@ -17,10 +17,10 @@
 #include "k1_kernels.cuh"
 
 #ifndef K1_RING_MINB
-#define K1_RING_MINB 2
+#define K1_RING_MINB 1
 #endif
 #ifndef K1_RING_FWD_MINB
-#define K1_RING_FWD_MINB 2
+#define K1_RING_FWD_MINB 1
 #endif
 
 namespace k1 {
@@ -140,6 +140,8 @@ __global__ void __launch_bounds__((NCW + 1) * 32, K1_RING_FWD_MINB) k1_fwd_ring_
     __shared__ __align__(8) uint64_t empty[STAGES];
     __shared__ FwdSmem<NC> sm;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    pdl_wait();
+    pdl_trigger();
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; ++s) {
             ring::bar_init(&full[s], 1);
@@ -222,14 +224,15 @@ __global__ void __launch_bounds__((NCW + 1) * 32, K1_RING_FWD_MINB) k1_fwd_ring_
         sm.split_prev[1] = split_prev[1];
     }
     fwd_flush_rows<T, NC, BAR, SHARD>(p, sm, count);
-#pragma unroll
-    for (int slot = 0; slot < 2; ++slot) {
-        const int64_t sr = split_row[slot];
-        if (sr < 0) continue;
-        const int64_t bf = block_of(sr * p.vpr, p.total, G);
-        const int64_t bl = block_of((sr + 1) * p.vpr - 1, p.total, G);
-        if (sm.split_prev[slot] == (unsigned)(bl - bf))
-            fwd_merge_split_row<T, NC, BAR, SHARD>(p, sr, sm.merge);
+    const int slot = tid >> 5;
+    if (slot < 2) {
+        const int64_t sr = slot == 0 ? split_row[0] : split_row[1];
+        if (sr >= 0) {
+            const int64_t bf = block_of(sr * p.vpr, p.total, G);
+            const int64_t bl = block_of((sr + 1) * p.vpr - 1, p.total, G);
+            const unsigned prev = slot == 0 ? sm.split_prev[0] : sm.split_prev[1];
+            if (prev == (unsigned)(bl - bf)) fwd_merge_split_row<T, SHARD>(p, sr);
+        }
     }
 }
 
@@ -245,6 +248,8 @@ __global__ void __launch_bounds__((NCW + 1) * 32, K1_RING_MINB) k1_bwd_ring_kern
     __shared__ __align__(8) uint64_t full[STAGES];
     __shared__ __align__(8) uint64_t empty[STAGES];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    pdl_wait();
+    pdl_trigger();
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; ++s) {
             ring::bar_init(&full[s], 1);
