@@ -309,6 +309,32 @@ int launch_backward(const char* fn, const void* logits, const Rows& L, const Row
     return check_launch(fn);
 }
 
+// ---------------------------------------------------------------------------------
+// Allocation-free forward: its split-row scratch is this file-scope device array, so the
+// entry point needs no workspace from the caller.  Every GPU that loads the library
+// holds the array until the process exits.  Every call on a device shares it.
+// ---------------------------------------------------------------------------------
+constexpr size_t kStaticScratchBytes = 256 * 1024;
+static __device__ __align__(256) unsigned char g_static_scratch[kStaticScratchBytes];
+
+// Device address of g_static_scratch on device `dev`, looked up once per device with
+// that device current (the symbol's name is only a host-side handle, not an address).
+int static_scratch_ptr(int dev, void** out) {
+    static std::mutex mu;
+    static void* ptrs[kMaxDevices] = {};
+    std::lock_guard<std::mutex> lock(mu);
+    if (ptrs[dev] == nullptr) {
+        void* p = nullptr;
+        cudaError_t e = cudaGetSymbolAddress(&p, g_static_scratch);
+        if (e != cudaSuccess || p == nullptr)
+            return fail(K1_ERR_CUDA, "cudaGetSymbolAddress(static scratch): %s",
+                        cudaGetErrorString(e));
+        ptrs[dev] = p;
+    }
+    *out = ptrs[dev];
+    return K1_OK;
+}
+
 int check_common(const char* fn, const void* logits, int dtype, const Rows& L) {
     if (dtype != K1_DTYPE_F32 && dtype != K1_DTYPE_F16 && dtype != K1_DTYPE_BF16)
         return fail(K1_ERR_UNSUPPORTED_DTYPE, "%s: logits dtype must be bf16, fp16, or fp32", fn);
@@ -373,6 +399,55 @@ int k1_fused_logprob_entropy_v1(const void* logits, int dtype, int64_t n_rows, i
         default:
             return launch_forward<float, false>(fn, logits, L, 0, targets, logprob, entropy, lse,
                                                 nullptr, workspace, workspace_bytes, s);
+    }
+}
+
+int k1_fused_logprob_entropy_v1_noalloc(const void* logits, int dtype, int64_t n_rows,
+                                        int64_t vocab, int64_t inner_rows, int64_t inner_stride,
+                                        int64_t outer_stride, const int64_t* targets,
+                                        float* logprob, float* entropy, float* lse,
+                                        void* stream) {
+    static const char* fn = "k1_fused_logprob_entropy_v1_noalloc";
+    Rows L{n_rows, vocab, inner_rows, inner_stride, outer_stride};
+    int rc = check_common(fn, logits, dtype, L);
+    if (rc) return rc;
+    if (n_rows == 0) return K1_OK;
+    if (!targets || !logprob || !entropy || !lse)
+        return fail(K1_ERR_INVALID_ARGUMENT, "%s: NULL targets or output pointer", fn);
+    int dev = 0, sms = 0;
+    rc = current_device(&dev);
+    if (rc) return rc;
+    rc = sm_count(dev, &sms);
+    if (rc) return rc;
+    // The scratch this device needs grows with its SM count, not with the problem size.
+    const size_t need = workspace_bytes_for(sms);
+    if (need > kStaticScratchBytes)
+        return fail(K1_ERR_WORKSPACE,
+                    "%s: this device (%d SMs) needs %zu bytes of scratch; the static scratch "
+                    "holds at most %zu bytes",
+                    fn, sms, need, kStaticScratchBytes);
+    void* ws = nullptr;
+    rc = static_scratch_ptr(dev, &ws);
+    if (rc) return rc;
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    // The tickets must start at zero; the previous call may not have left them so (it
+    // may still be running on another stream, which is a documented race, or have been
+    // interrupted).  Clearing is stream-ordered and allocates nothing.
+    const size_t gmax = (size_t)sms * kMaxBlocksPerSm;
+    cudaError_t e = cudaMemsetAsync(reinterpret_cast<char*>(ws) + 2 * gmax * sizeof(k1::RowPartial),
+                                    0, gmax * sizeof(unsigned), s);
+    if (e != cudaSuccess)
+        return fail(K1_ERR_CUDA, "%s: clearing the static scratch: %s", fn, cudaGetErrorString(e));
+    switch (dtype) {
+        case K1_DTYPE_BF16:
+            return launch_forward<__nv_bfloat16, false>(fn, logits, L, 0, targets, logprob, entropy,
+                                                        lse, nullptr, ws, kStaticScratchBytes, s);
+        case K1_DTYPE_F16:
+            return launch_forward<__half, false>(fn, logits, L, 0, targets, logprob, entropy, lse,
+                                                 nullptr, ws, kStaticScratchBytes, s);
+        default:
+            return launch_forward<float, false>(fn, logits, L, 0, targets, logprob, entropy, lse,
+                                                nullptr, ws, kStaticScratchBytes, s);
     }
 }
 

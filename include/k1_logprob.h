@@ -113,6 +113,26 @@ int k1_fused_logprob_entropy_v1(const void* logits, int dtype, int64_t n_rows, i
                                 void* stream);
 
 /*
+ * Forward that allocates nothing and takes no workspace: the same kernel and results as
+ * k1_fused_logprob_entropy_v1, with its split-row scratch in a 256 KiB array that the
+ * library defines in device memory (held on every GPU that loads the library until the
+ * process exits).  For callers that cannot call cudaMalloc or hand out device memory of
+ * their own -- e.g. a plugin inside a host framework whose memory pool is the only
+ * allocator, or latency-critical code that must avoid cudaMalloc's implicit device
+ * synchronisation.  Fails with K1_ERR_WORKSPACE if a device needs more scratch than the
+ * array holds (it needs 2 x 24 + 4 bytes per resident block, about 61 KiB on 148 SMs).
+ * The first call on a device looks up the array's device address with that device
+ * current; make that first call before any stream capture.  Each call clears the part
+ * of the array that must start at zero.  All calls on a device share the array: calls
+ * that may overlap on the GPU (different streams, concurrent host threads) race and must
+ * be serialised by the caller.  No counterpart in the reference.
+ */
+int k1_fused_logprob_entropy_v1_noalloc(const void* logits, int dtype, int64_t n_rows,
+                                        int64_t vocab, int64_t inner_rows, int64_t inner_stride,
+                                        int64_t outer_stride, const int64_t* targets,
+                                        float* logprob, float* entropy, float* lse, void* stream);
+
+/*
  * Forward, one thread per row, fp64 accumulation.  A simple correctness anchor,
  * never fast.  Replaces fused_logprob_entropy_naive
  * (reference csrc/fused_logprob.cu:405-458, bound at csrc/bindings.cpp:18-20).
