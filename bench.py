@@ -52,6 +52,8 @@ CONFIGS = {
                     dtype=torch.float16, scale=2.0, window=False, spikes=True),
     "c4-fp32": dict(workload="baseline-config-4: stress, fp32", B=1, S=8192, V=128256,
                     dtype=torch.float32, scale=2.0, window=False, spikes=True),
+    "c5": dict(workload="baseline-config-5: vocab-parallel LM head [32768, 256000]", B=1,
+               S=32768, V=256000, dtype=torch.bfloat16, scale=3.0, window=False),
 }
 DTYPE_NAME = {torch.bfloat16: "bf16", torch.float16: "fp16", torch.float32: "fp32"}
 
@@ -392,7 +394,7 @@ def ours_arm(args, cfg, rank, local_rank, world):
                    "parallelism": f"row-sharded x{world} (no collective)",
                    "l2": (f"inputs larger than L2: {logits.numel() * esize / 2**20:.0f} MiB "
                           f"logits read and written per step vs {L2_BYTES // 2**20} MiB L2")},
-        "roofline": {"bound": "hbm", "kernel": "k1_bwd_kernel", "achieved": round(achieved, 1),
+        "roofline": {"bound": "hbm", "kernel": "k1_bwd_ring_kernel", "achieved": round(achieved, 1),
                      "peak": peak, "unit": "GB/s", "frac": round(achieved / peak, 4),
                      "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs, copy)",
                      "algorithmic_bytes_per_launch": bwd_bytes,
@@ -408,6 +410,83 @@ def ours_arm(args, cfg, rank, local_rank, world):
     print(json.dumps(out), flush=True)
 
 
+def vocab_arm(args, cfg, rank, local_rank, world):
+    """Vocab-parallel K1 (tensor-parallel LM head layout): rank k holds columns
+    vocab_shard(V, world, k) of every row; forward = shard partials + one all-gather + merge,
+    backward local.  The total problem is fixed (strong scaling)."""
+    import torch.distributed as dist
+
+    from kernel_opt import parallel
+
+    device = torch.device("cuda", local_rank)
+    torch.cuda.set_device(device)
+    os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+    os.environ.setdefault("MASTER_PORT", "29561")
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=device,
+                            timeout=datetime.timedelta(seconds=300))
+    N, V, dt = cfg["B"] * cfg["S"], cfg["V"], cfg["dtype"]
+    esize = torch.tensor([], dtype=dt).element_size()
+    cols = parallel.vocab_shard(V, world, rank)
+    Vr = cols.stop - cols.start
+    gen = torch.Generator(device=device).manual_seed(7000 + rank)
+    xs = torch.empty((N, Vr), dtype=dt, device=device)
+    for a in range(0, N, 1024):
+        b = min(N, a + 1024)
+        xs[a:b] = (torch.randn((b - a, Vr), generator=gen, device=device) * cfg["scale"]).to(dt)
+    tg = torch.Generator(device=device).manual_seed(99)
+    targets = torch.randint(0, V, (N,), generator=tg, device=device)
+    g_lp = torch.full((N,), -1.0 / N, device=device)
+    g_h = torch.full((N,), -0.01 / N, device=device)
+    stream = torch.cuda.current_stream(device)
+
+    def step():
+        x = xs.detach().requires_grad_(True)
+        lp, h, _l = parallel.vocab_parallel_fused_logprob_entropy(x, targets, cols.start)
+        (d,) = torch.autograd.grad((lp, h), x, (g_lp, g_h))
+        return d
+
+    def barrier():
+        dist.barrier(device_ids=[local_rank])
+        torch.cuda.synchronize(device)
+
+    for _ in range(max(3, args.warmup)):
+        step()
+    barrier()
+    K = args.steps
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(device) as clocks:
+        barrier()
+        start.record(stream)
+        for _ in range(K):
+            step()
+        stop.record(stream)
+        barrier()
+    t = torch.tensor([start.elapsed_time(stop)], device=device, dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    max_ms = float(t.item())
+    barrier()
+    dist.destroy_process_group()
+    if rank != 0:
+        return
+    fwd, bwd = algorithmic_bytes(N, V, esize)
+    value = (fwd + bwd) * K / (max_ms / 1e3) / 1e9
+    peak, peak_kind = measured_peak_gbs()
+    out = {
+        "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world, "steps": K,
+        "warmup": args.warmup, "ms_per_step": round(max_ms / K, 4), "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": DTYPE_NAME[dt], "data": "synthetic",
+        "rows_per_s": round(N * K / (max_ms / 1e3), 1),
+        "pct_of_peak_per_gpu": round(100 * value / world / peak, 2),
+        "config": {"workload": cfg["workload"], "rows": N, "vocab": V, "vocab_per_gpu": Vr,
+                   "parallelism": f"vocab-parallel x{world}: one all-gather of [N,4] float64 "
+                                  "per forward, local backward"},
+        "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs, copy)",
+        "gpu_launches": 4 * K,
+        "clocks": clocks.summary(),
+    }
+    print(json.dumps(out), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
     ap.add_argument("--gpus", type=int, default=1)
@@ -416,6 +495,8 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--config", choices=sorted(CONFIGS), default="c2")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--mode", choices=["rows", "vocab"], default="rows",
+                    help="rows: row-sharded (default); vocab: vocab-parallel (config c5)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -423,6 +504,8 @@ def main():
     cfg = CONFIGS[args.config]
     if args.impl == "reference":
         reference_arm(args, cfg, rank, world)
+    elif args.mode == "vocab":
+        vocab_arm(args, CONFIGS["c5"] if args.config == "c2" else cfg, rank, local_rank, world)
     else:
         ours_arm(args, cfg, rank, local_rank, world)
 

@@ -10,8 +10,8 @@
 // all).  A wait that runs out sets the device word k1_ring_error and the thread stops
 // waiting; the producer drains every copy it issued before it exits.  No wait depends
 // on another block or another GPU.  Bulk copies are plain global -> shared copies of this
-// GPU's memory (no multicast); source and size are multiples of 16 bytes on the vector
-// path.
+// GPU's memory into this block's own shared memory; source and size are multiples of 16
+// bytes on the vector path.
 #pragma once
 
 #include "k1_kernels.cuh"
