@@ -254,6 +254,7 @@ def reference_arm(args, cfg, rank, world):
     n_rows = b_use * S
     fwd, bwd = algorithmic_bytes(n_rows, V, esize)
     value = (fwd + bwd) * args.steps / el / 1e9
+    ref_gpu = time_reference_k1_gpu(cfg)
     out = {
         "metric": METRIC, "value": round(value, 4), "unit": UNIT, "impl": "reference",
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
@@ -270,7 +271,54 @@ def reference_arm(args, cfg, rank, world):
         "e2e": {"value": round(value, 4), "unit": UNIT, "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
+    if ref_gpu is not None:
+        out["reference_k1_sm100a"] = ref_gpu
     print(json.dumps(out), flush=True)
+
+
+def time_reference_k1_gpu(cfg, iters=20):
+    """The reference's own CUDA K1 (csrc/fused_logprob.cu, rebuilt for sm_100a by
+    oracle/build_ref.py) on the same workload shape, timed with CUDA events (median).
+    Informational: it is the reference's GPU kernel, not its CPU path."""
+    try:
+        if not torch.cuda.is_available():
+            return None
+        from oracle import reference_k1
+        if reference_k1.load() is None:
+            return {"unavailable": "oracle/_ref build absent"}
+    except Exception as e:  # pragma: no cover
+        return {"unavailable": f"{type(e).__name__}: {e}"[:200]}
+    dev = torch.device("cuda", 0)
+    B, S, V, dt = cfg["B"], cfg["S"], cfg["V"], cfg["dtype"]
+    N = B * S
+    gen = torch.Generator(device=dev).manual_seed(4321)
+    x = (torch.randn((N, V), generator=gen, device=dev) * cfg["scale"]).to(dt)
+    t = torch.randint(0, V, (N,), generator=gen, device=dev)
+    gl = torch.full((N,), -1.0 / N, device=dev)
+    gh = torch.full((N,), -0.01 / N, device=dev)
+    gz = torch.zeros(N, device=dev)
+    lp, h, l = reference_k1.forward(x, t)
+    d = reference_k1.backward(x, t, l, h, gl, gh, gz)
+    tf, tb = [], []
+    for _ in range(iters):
+        a, b, c = (torch.cuda.Event(enable_timing=True) for _ in range(3))
+        a.record()
+        lp, h, l = reference_k1.forward(x, t)
+        b.record()
+        d = reference_k1.backward(x, t, l, h, gl, gh, gz)
+        c.record()
+        torch.cuda.synchronize()
+        tf.append(a.elapsed_time(b))
+        tb.append(b.elapsed_time(c))
+    esize = torch.tensor([], dtype=dt).element_size()
+    fwd, bwd = algorithmic_bytes(N, V, esize)
+    mf, mb = statistics.median(tf), statistics.median(tb)
+    del x, d
+    return {"fwd_ms": round(mf, 4), "bwd_ms": round(mb, 4),
+            "fwd_gbs": round(fwd / (mf / 1e3) / 1e9, 1), "bwd_gbs": round(bwd / (mb / 1e3) / 1e9, 1),
+            "fwd_bwd_gbs": round((fwd + bwd) / ((mf + mb) / 1e3) / 1e9, 1),
+            "note": "reference csrc/fused_logprob.cu v1 kernels rebuilt for sm_100a "
+                    "(oracle/build_ref.py), same shape, CUDA events, median of %d" % iters}
 
 
 def ours_arm(args, cfg, rank, local_rank, world):

@@ -89,6 +89,66 @@ class _FusedLogprobEntropy(torch.autograd.Function):
         return d_logits, None
 
 
+# ---------------------------------------------------------------------------------------
+# torch.library registration: under torch.compile K1 is one opaque op with a fake (meta)
+# implementation and an autograd formula, so compiled graphs contain it without a graph
+# break.  (The reference's pybind call graph-breaks: REPORT.md:315-318.)
+# ---------------------------------------------------------------------------------------
+@torch.library.custom_op("kernel_opt::fused_logprob_entropy_fwd", mutates_args=())
+def _fwd_op(logits: torch.Tensor, targets: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor,
+                                                                   torch.Tensor]:
+    targets = targets.contiguous()
+    logprob, entropy, lse = _alloc_outputs(targets)
+    _C.fused_logprob_entropy_v1(logits, targets, logprob, entropy, lse)
+    return logprob, entropy, lse
+
+
+@_fwd_op.register_fake
+def _(logits, targets):
+    return tuple(torch.empty(targets.shape, device=targets.device, dtype=torch.float32)
+                 for _ in range(3))
+
+
+@torch.library.custom_op("kernel_opt::fused_logprob_entropy_bwd", mutates_args=())
+def _bwd_op(logits: torch.Tensor, targets: torch.Tensor, lse: torch.Tensor,
+            entropy: torch.Tensor, g_logp: torch.Tensor | None, g_ent: torch.Tensor | None,
+            g_lse: torch.Tensor | None) -> torch.Tensor:
+    d_logits = torch.empty_like(logits)
+    _C.fused_logprob_entropy_v1_backward(logits, targets.contiguous(), lse, entropy,
+                                         g_logp, g_ent, g_lse, d_logits)
+    return d_logits
+
+
+@_bwd_op.register_fake
+def _(logits, targets, lse, entropy, g_logp, g_ent, g_lse):
+    return torch.empty_like(logits)
+
+
+def _op_setup_context(ctx, inputs, output):
+    logits, targets = inputs
+    _logprob, entropy, lse = output
+    ctx.save_for_backward(logits, targets, lse, entropy)
+
+
+def _op_backward(ctx, g_logp, g_ent, g_lse):
+    logits, targets, lse, entropy = ctx.saved_tensors
+
+    def _prep(g):
+        return None if g is None else g.to(torch.float32).contiguous()
+
+    return _bwd_op(logits, targets, lse, entropy, _prep(g_logp), _prep(g_ent), _prep(g_lse)), None
+
+
+_fwd_op.register_autograd(_op_backward, setup_context=_op_setup_context)
+
+
+def fused_logprob_entropy_op(logits: torch.Tensor, targets: torch.Tensor):
+    """K1 through the registered custom op `kernel_opt::fused_logprob_entropy_fwd` (same
+    results and gradients as `fused_logprob_entropy`)."""
+    _check_inputs(logits, targets)
+    return _fwd_op(logits, targets)
+
+
 def fused_logprob_entropy(logits: torch.Tensor, targets: torch.Tensor):
     """K1 (production), autograd-aware.  Reference ops.py:92-111.
 
@@ -107,6 +167,9 @@ def fused_logprob_entropy(logits: torch.Tensor, targets: torch.Tensor):
             entropy[i] = -sum_v softmax(logits[i])[v] * log_softmax(logits[i])[v]
             lse[i]     = logsumexp(logits[i])
 
-    `targets` has no gradient.
+    `targets` has no gradient.  Under torch.compile the call goes through the registered
+    custom op (one node in the graph, no graph break); eagerly it is an autograd.Function.
     """
+    if torch.compiler.is_compiling():
+        return fused_logprob_entropy_op(logits, targets)
     return _FusedLogprobEntropy.apply(logits, targets)

@@ -161,3 +161,32 @@ def test_no_ring_wait_ran_out():
     autograd_grad(x, t, grads_like((64,), seed=61))
     torch.cuda.synchronize()
     assert _C.ring_status() == 0
+
+
+def test_custom_op_opcheck():
+    """torch.library.opcheck: schema, fake tensor, autograd registration, AOT dispatch."""
+    from kernel_opt import ops
+    x = seeded_logits((2, 4, 1000), torch.float32, 1.0, seed=70).cuda().requires_grad_(True)
+    t = seeded_targets((2, 4), 1000, seed=71).cuda()
+    torch.library.opcheck(ops._fwd_op, (x, t))
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_compile_fullgraph_no_graph_break(dtype):
+    """With the custom op, a compiled loss containing K1 is one graph (fullgraph=True would
+    raise on a graph break) and matches eager in value and gradient."""
+    x0 = seeded_logits((2, 8, 4096), dtype, 1.0, seed=72).cuda()
+    t = seeded_targets((2, 8), 4096, seed=73).cuda()
+
+    def loss_fn(x, t):
+        lp, h, _l = kernel_opt.fused_logprob_entropy(x, t)
+        return (lp + 0.1 * h).sum()
+
+    xe = x0.clone().requires_grad_(True)
+    le = loss_fn(xe, t)
+    le.backward()
+    xc = x0.clone().requires_grad_(True)
+    lc = torch.compile(loss_fn, backend="aot_eager", fullgraph=True)(xc, t)
+    lc.backward()
+    torch.testing.assert_close(lc, le, rtol=1e-6, atol=1e-6)
+    torch.testing.assert_close(xc.grad, xe.grad, rtol=0, atol=0)

@@ -66,3 +66,15 @@ def test_completion_window_is_a_strided_view():
     assert w.data_ptr() == base[:, 4:10].data_ptr()
     assert w.stride() == (55, 5, 1) and not w.is_contiguous()
     torch.testing.assert_close(w, base[:, :-1][:, -6:])
+
+
+def test_custom_op_fake_shapes():
+    """The registered op's fake implementation (used by torch.compile tracing)."""
+    from kernel_opt import ops
+    x = torch.empty(2, 3, 40, device="meta", dtype=torch.bfloat16)
+    t = torch.empty(2, 3, device="meta", dtype=torch.int64)
+    lp, h, l = ops._fwd_op(x, t)
+    assert all(o.shape == (2, 3) and o.dtype == torch.float32 for o in (lp, h, l))
+    d = ops._bwd_op(x, t, l, h, lp, None, None)
+    assert d.shape == x.shape and d.dtype == x.dtype
+    assert hasattr(torch.ops.kernel_opt, "fused_logprob_entropy_fwd")
