@@ -6,6 +6,7 @@
 // validation is on raw pointers / sizes (the torch-facing checks live in the binding
 // layer, k1_torch_binding.cpp), and every kernel gets a grid of
 // (SM count) x (resident blocks per SM) blocks that split the flattened work evenly.
+#include <algorithm>
 #include <atomic>
 #include <cstdarg>
 #include <cstdio>

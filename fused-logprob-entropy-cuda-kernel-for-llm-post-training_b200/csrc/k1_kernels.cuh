@@ -17,6 +17,16 @@
 
 namespace k1 {
 
+// Block pieces: the flattened unit range [0, total) is cut into G equal contiguous pieces,
+// piece b = [floor(b * total / G), floor((b + 1) * total / G)).
+__device__ __forceinline__ int64_t piece_start(int64_t b, int64_t total, int64_t G) {
+    return b * total / G;
+}
+// Block whose piece holds unit u.
+__device__ __forceinline__ int64_t block_of(int64_t u, int64_t total, int64_t G) {
+    return ((u + 1) * G + total - 1) / total - 1;
+}
+
 struct FwdParams {
     const void* logits;
     int64_t n_rows;
@@ -32,7 +42,6 @@ struct FwdParams {
     k1_partial* partials;  // shard mode output
     RowPartial* ws_part;   // 2 * gridDim.x slots
     unsigned* ws_ticket;   // gridDim.x counters, zero between calls
-    unsigned* ws_error;    // set to nonzero if a bounded wait ran out (bulk-copy ring)
 };
 
 struct BwdParams {
@@ -51,14 +60,7 @@ struct BwdParams {
     const float* g_logp;
     const float* g_ent;
     const float* g_lse;
-    unsigned* ws_error;  // set to nonzero if a bounded wait ran out (bulk-copy ring)
 };
-
-// Block that owns flattened unit u when `total` units are cut into G equal pieces
-// (piece b = [floor(b * total / G), floor((b + 1) * total / G))).
-__device__ __forceinline__ int64_t block_of(int64_t u, int64_t total, int64_t G) {
-    return ((u + 1) * G + total - 1) / total - 1;
-}
 
 // ---------------------------------------------------------------------------------
 // Forward: per-chunk work of one thread
@@ -384,7 +386,7 @@ __device__ __forceinline__ void fwd_merge_split_row(const FwdParams& p, int64_t 
     acc.m = -INFINITY;
     acc.pad = 0.f;
     for (int64_t c = bf + lane; c <= bl; c += 32) {
-        const int64_t fr = (c * p.total / G) / p.vpr;
+        const int64_t fr = piece_start(c, p.total, G) / p.vpr;
         const RowPartial* q = p.ws_part + 2 * c + (r == fr ? 0 : 1);
         RowPartial qq;
         qq.z = __ldcg(&q->z);
@@ -393,15 +395,19 @@ __device__ __forceinline__ void fwd_merge_split_row(const FwdParams& p, int64_t 
         qq.pad = 0.f;
         acc = merge_partials(acc, qq);
     }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-        RowPartial other;
-        other.z = __shfl_xor_sync(0xffffffffu, acc.z, o);
-        other.t = __shfl_xor_sync(0xffffffffu, acc.t, o);
-        other.m = __shfl_xor_sync(0xffffffffu, acc.m, o);
-        other.pad = 0.f;
-        acc = merge_partials(acc, other);
+    // warp merge: common maximum first, one scale factor per lane, then plain fp64 sums
+    const float M = warp_max_nan(acc.m);
+    double zc = 0.0, tc = 0.0;
+    if (acc.m != -INFINITY) {
+        const float dm = acc.m - M;  // <= 0, NaN if either is NaN
+        const float sc = (dm == 0.f) ? 1.f : ex2(dm * kLog2e);
+        zc = (double)sc * acc.z;
+        tc = (double)sc * (acc.t + (double)dm * acc.z);
     }
+    acc.z = warp_sum(zc);
+    acc.t = warp_sum(tc);
+    acc.m = M;
+    if (M == -INFINITY) acc.z = acc.t = 0.0;
     if (lane == 0) {
         if constexpr (SHARD) {
             k1_partial out;
@@ -427,8 +433,8 @@ __global__ void __launch_bounds__(THREADS, K1_FWD_MINB) k1_fwd_kernel(FwdParams 
     pdl_trigger();
     const int tid = threadIdx.x;
     const int64_t G = gridDim.x, b = blockIdx.x;
-    const int64_t start0 = b * p.total / G;
-    const int64_t end = (b + 1) * p.total / G;
+    const int64_t start0 = piece_start(b, p.total, G);
+    const int64_t end = piece_start(b + 1, p.total, G);
     int64_t start = start0;
     int64_t r = start / p.vpr;
     int64_t j0 = start - r * p.vpr;
@@ -475,8 +481,7 @@ __global__ void __launch_bounds__(THREADS, K1_FWD_MINB) k1_fwd_kernel(FwdParams 
             if (tid == 0) {
                 p.ws_part[2 * b + slot] = part;
                 __threadfence();
-                const int64_t bf = block_of(r * p.vpr, p.total, G);
-                split_prev[slot] = atomicAdd(p.ws_ticket + bf, 1u);
+                split_prev[slot] = atomicAdd(p.ws_ticket + block_of(r * p.vpr, p.total, G), 1u);
             }
         }
         start += j1 - j0;

@@ -151,7 +151,7 @@ __global__ void __launch_bounds__((NCW + 1) * 32, K1_RING_FWD_MINB) k1_fwd_ring_
     }
     __syncthreads();
     const int64_t G = gridDim.x, b = blockIdx.x;
-    const int64_t start = b * p.total / G, end = (b + 1) * p.total / G;
+    const int64_t start = piece_start(b, p.total, G), end = piece_start(b + 1, p.total, G);
     if (warp == NCW) {
         if (lane == 0)
             ring::produce<STAGES, SV>(p.logits, p.lay, (int)sizeof(T), p.vpr, start, end, ring_buf,
