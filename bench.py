@@ -458,6 +458,175 @@ def ours_arm(args, cfg, rank, local_rank, world):
     print(json.dumps(out), flush=True)
 
 
+def grpo_arm(args, cfg, rank, local_rank, world):
+    """The GRPO loss block on config 3: model logits [B, L, V] (the parent) -> per-token
+    logps / entropies of the completion window at temperature T -> gradient w.r.t. the
+    parent.  Two implementations on identical inputs, one GPU each (rows shard by batch
+    element, no collective):
+      fused   -- kernel_opt.grpo window node: scaled K1 forward on the strided window, one
+                 backward launch writing the parent-shaped gradient;
+      unfused -- the reference trainer's sequence (trainer.py:96-127): slice, in-place
+                 division by T, K1, autograd backward through the division and the slices
+                 (our K1 inside, one launch on the window).
+    Peak extra device memory of one step is reported for both and for the fused node with
+    inplace_backward (which reuses the logits' storage for the gradient)."""
+    import torch.distributed as dist
+
+    import kernel_opt
+    from kernel_opt import grpo
+
+    device = torch.device("cuda", local_rank)
+    torch.cuda.set_device(device)
+    if world > 1:
+        dist.init_process_group("nccl", rank=rank, world_size=world, device_id=device,
+                                timeout=datetime.timedelta(seconds=300))
+    if not cfg["window"]:
+        cfg = CONFIGS["c3"]
+    B, S, V, dt = cfg["B"], cfg["S"], cfg["V"], cfg["dtype"]
+    T = 0.7
+    esize = torch.tensor([], dtype=dt).element_size()
+    window, targets, g_lp, g_h = make_workload(cfg, device, seed=4321 + rank)
+    parent = torch.as_strided(window, (B, S + 1, V), ((S + 1) * V, V, 1), 0)
+    assert grpo.completion_window(parent, S).data_ptr() == window.data_ptr()
+    N = B * S
+    scale = grpo.temperature_scale(T)
+    stream = torch.cuda.current_stream(device)
+    # algorithmic bytes: forward reads the window; backward reads the window and writes
+    # the whole parent-shaped gradient (window rows + the zeroed last row per sequence)
+    fwd_bytes = N * V * esize + N * 20
+    bwd_bytes = N * V * esize + B * (S + 1) * V * esize + N * 16
+    step_bytes = fwd_bytes + bwd_bytes
+
+    def fused(x):
+        lp, h, _ = grpo._WindowLogprobEntropy.apply(x, targets, S, scale, False)
+        return lp, h
+
+    def unfused_fwd(y):
+        w = grpo.completion_window(y, S)
+        w.div_(T)
+        lp, h, _ = kernel_opt.fused_logprob_entropy(w, targets)
+        return lp, h
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local_rank])
+        torch.cuda.synchronize(device)
+
+    def run(kind, K, timed):
+        ev = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(K)]
+        for i in range(K):
+            x = parent.detach().requires_grad_(True)
+            y = x.clone() if kind == "unfused" else x  # the clone stands in for the model
+            ev[i][0].record(stream)                    # output that div_ overwrites
+            lp, h = unfused_fwd(y) if kind == "unfused" else fused(y)
+            ev[i][1].record(stream)
+            (d,) = torch.autograd.grad((lp, h), x, (g_lp, g_h))
+            ev[i][2].record(stream)
+            del d, lp, h, x, y
+        barrier()
+        if not timed:
+            return None
+        f = [e[0].elapsed_time(e[1]) for e in ev]
+        b = [e[1].elapsed_time(e[2]) for e in ev]
+        return statistics.mean(f), statistics.mean(b)
+
+    def check_equal():
+        x = parent.detach().requires_grad_(True)
+        a = fused(x)
+        (da,) = torch.autograd.grad(a, x, (g_lp, g_h))
+        x2 = parent.detach().requires_grad_(True)
+        b = unfused_fwd(x2.clone())
+        (db,) = torch.autograd.grad(b, x2, (g_lp, g_h))
+        same = all(torch.equal(u.detach(), v.detach()) for u, v in zip(a, b)) and torch.equal(da, db)
+        del x, x2, a, b, da, db
+        return same
+
+    class _ModelOutput(torch.autograd.Function):
+        """Stand-in for the LM head: returns a copy of the parent as a non-leaf tensor and
+        passes the gradient through without allocating."""
+
+        @staticmethod
+        def forward(ctx, src):
+            return src.clone()
+
+        @staticmethod
+        def backward(ctx, g):
+            return g
+
+    def peak_extra(block):
+        """Device memory the loss block allocates beyond the model output it consumes,
+        forward through backward (peak, bytes)."""
+        src = parent.detach().requires_grad_(True)
+        y = _ModelOutput.apply(src)
+        torch.cuda.synchronize(device)
+        torch.cuda.reset_peak_memory_stats(device)
+        base = torch.cuda.memory_allocated(device)
+        lp, h = block(y)
+        d = torch.autograd.grad((lp, h), src, (g_lp, g_h))
+        torch.cuda.synchronize(device)
+        extra = torch.cuda.max_memory_allocated(device) - base
+        del d, lp, h, y, src
+        return extra
+
+    def fused_block(inplace):
+        def f(y):
+            lp, h, _ = grpo._WindowLogprobEntropy.apply(y, targets, S, scale, inplace)
+            return lp, h
+        return f
+
+    for kind in ("fused", "unfused"):
+        run(kind, max(3, args.warmup), False)
+    bit_equal = check_equal()
+    K = args.steps
+    with ClockSampler(device) as clocks:
+        barrier()
+        t0 = torch.cuda.Event(enable_timing=True)
+        t1 = torch.cuda.Event(enable_timing=True)
+        t0.record(stream)
+        fused_fb = run("fused", K, True)
+        t1.record(stream)
+        barrier()
+    unfused_fb = run("unfused", K, True)
+    total = torch.tensor([t0.elapsed_time(t1)], device=device, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(total, op=dist.ReduceOp.MAX)
+    max_ms = float(total.item())
+    mem = {"fused": peak_extra(fused_block(False)), "fused_inplace": peak_extra(fused_block(True)),
+           "unfused": peak_extra(unfused_fwd)}
+    if world > 1:
+        dist.barrier(device_ids=[local_rank])
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    peak, peak_kind = measured_peak_gbs()
+    value = step_bytes * K * world / (max_ms / 1e3) / 1e9
+    f_ms, b_ms = fused_fb
+    uf_ms, ub_ms = unfused_fb
+    out = {
+        "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world, "steps": K,
+        "warmup": args.warmup, "ms_per_step": round(max_ms / K, 4), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": DTYPE_NAME[dt], "data": "synthetic",
+        "rows_per_s": round(N * K * world / (max_ms / 1e3), 1),
+        "pct_of_peak": round(100 * value / world / peak, 2),
+        "config": {"workload": "GRPO loss block on " + cfg["workload"], "global_batch": B * world,
+                   "seq_len": S, "vocab": V, "temperature": T,
+                   "parallelism": f"row-sharded x{world} (no collective)",
+                   "l2": (f"inputs larger than L2: {parent.numel() * esize / 2**20:.0f} MiB "
+                          f"parent logits vs {L2_BYTES // 2**20} MiB L2")},
+        "fused": {"fwd_ms": round(f_ms, 4), "bwd_ms": round(b_ms, 4),
+                  "fwd_gbs": round(fwd_bytes / (f_ms / 1e3) / 1e9, 1),
+                  "bwd_gbs": round(bwd_bytes / (b_ms / 1e3) / 1e9, 1)},
+        "unfused_reference_sequence": {"fwd_ms": round(uf_ms, 4), "bwd_ms": round(ub_ms, 4)},
+        "speedup_fused_vs_unfused": round((uf_ms + ub_ms) / (f_ms + b_ms), 3),
+        "bit_identical": bit_equal,
+        "peak_extra_bytes_per_step": mem,
+        "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs, copy)",
+        "gpu_launches": 2 * K,
+        "clocks": clocks.summary(),
+    }
+    print(json.dumps(out), flush=True)
+
+
 def vocab_arm(args, cfg, rank, local_rank, world):
     """Vocab-parallel K1 (tensor-parallel LM head layout): rank k holds columns
     vocab_shard(V, world, k) of every row; forward = shard partials + one all-gather + merge,
@@ -543,8 +712,9 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--config", choices=sorted(CONFIGS), default="c2")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--mode", choices=["rows", "vocab"], default="rows",
-                    help="rows: row-sharded (default); vocab: vocab-parallel (config c5)")
+    ap.add_argument("--mode", choices=["rows", "vocab", "grpo"], default="rows",
+                    help="rows: row-sharded (default); vocab: vocab-parallel (config c5); "
+                         "grpo: the GRPO loss block on config c3, fused vs unfused")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -552,6 +722,8 @@ def main():
     cfg = CONFIGS[args.config]
     if args.impl == "reference":
         reference_arm(args, cfg, rank, world)
+    elif args.mode == "grpo":
+        grpo_arm(args, cfg, rank, local_rank, world)
     elif args.mode == "vocab":
         vocab_arm(args, CONFIGS["c5"] if args.config == "c2" else cfg, rank, local_rank, world)
     else:

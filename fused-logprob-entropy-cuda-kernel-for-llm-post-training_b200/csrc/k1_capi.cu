@@ -204,11 +204,11 @@ int grid_for(Kernel kernel, int dev, int64_t total, int64_t min_units, int64_t* 
     return K1_OK;
 }
 
-template <typename T, bool SHARD>
+template <typename T, bool SHARD, bool SCALED = false>
 int launch_forward(const char* fn, const void* logits, const Rows& L, int64_t col_offset,
                    const int64_t* targets, float* logprob, float* entropy, float* lse,
                    k1_partial* partials, void* workspace, size_t workspace_bytes,
-                   cudaStream_t stream) {
+                   cudaStream_t stream, float scale = 1.f) {
     int dev = 0;
     int rc = current_device(&dev);
     if (rc) return rc;
@@ -236,12 +236,13 @@ int launch_forward(const char* fn, const void* logits, const Rows& L, int64_t co
     p.entropy = entropy;
     p.lse = lse;
     p.partials = partials;
+    p.scale = SCALED ? scale : 1.f;
     const size_t gmax = (size_t)sms * kMaxBlocksPerSm;
     p.ws_part = reinterpret_cast<k1::RowPartial*>(workspace);
     p.ws_ticket = reinterpret_cast<unsigned*>(reinterpret_cast<char*>(workspace) +
                                               2 * gmax * sizeof(k1::RowPartial));
     int64_t grid = 1;
-    if (vec && kRingFwd) {
+    if (vec && kRingFwd && !SCALED) {
         auto kern = k1::k1_fwd_ring_kernel<T, kRingWarps, kRingStages, kRingBytes, SHARD>;
         const int threads = (kRingWarps + 1) * 32;
         const size_t smem = (size_t)kRingStages * kRingBytes;
@@ -249,12 +250,12 @@ int launch_forward(const char* fn, const void* logits, const Rows& L, int64_t co
         if (rc) return rc;
         launch(kern, grid, threads, smem, stream, p);
     } else if (vec) {
-        auto kern = k1::k1_fwd_kernel<T, kFwdThreads, kUnroll, true, SHARD>;
+        auto kern = k1::k1_fwd_kernel<T, kFwdThreads, kUnroll, true, SHARD, SCALED>;
         rc = grid_for(kern, dev, p.total, kMinUnitsPerBlockVec, &grid, kFwdThreads);
         if (rc) return rc;
         launch(kern, grid, kFwdThreads, 0, stream, p);
     } else {
-        auto kern = k1::k1_fwd_kernel<T, kFwdThreads, kUnroll, false, SHARD>;
+        auto kern = k1::k1_fwd_kernel<T, kFwdThreads, kUnroll, false, SHARD, SCALED>;
         rc = grid_for(kern, dev, p.total, kMinUnitsPerBlockScalar, &grid, kFwdThreads);
         if (rc) return rc;
         launch(kern, grid, kFwdThreads, 0, stream, p);
@@ -262,11 +263,11 @@ int launch_forward(const char* fn, const void* logits, const Rows& L, int64_t co
     return check_launch(fn);
 }
 
-template <typename T>
+template <typename T, bool SCALED = false>
 int launch_backward(const char* fn, const void* logits, const Rows& L, const Rows& D,
                     int64_t col_offset, const int64_t* targets, const float* lse,
                     const float* entropy, const float* g_logp, const float* g_ent,
-                    const float* g_lse, void* d_logits, cudaStream_t stream) {
+                    const float* g_lse, void* d_logits, cudaStream_t stream, float scale = 1.f) {
     int dev = 0;
     int rc = current_device(&dev);
     if (rc) return rc;
@@ -288,21 +289,22 @@ int launch_backward(const char* fn, const void* logits, const Rows& L, const Row
     p.g_logp = g_logp;
     p.g_ent = g_ent;
     p.g_lse = g_lse;
+    p.scale = SCALED ? scale : 1.f;
     int64_t grid = 1;
     if (vec && kRing) {
-        auto kern = k1::k1_bwd_ring_kernel<T, kRingWarps, kRingStages, kRingBytes>;
+        auto kern = k1::k1_bwd_ring_kernel<T, kRingWarps, kRingStages, kRingBytes, SCALED>;
         const int threads = (kRingWarps + 1) * 32;
         const size_t smem = (size_t)kRingStages * kRingBytes;
         rc = grid_for(kern, dev, p.total, kMinUnitsPerBlockVec, &grid, threads, smem);
         if (rc) return rc;
         launch(kern, grid, threads, smem, stream, p);
     } else if (vec) {
-        auto kern = k1::k1_bwd_kernel<T, kThreads, kUnrollBwd, true>;
+        auto kern = k1::k1_bwd_kernel<T, kThreads, kUnrollBwd, true, SCALED>;
         rc = grid_for(kern, dev, p.total, kMinUnitsPerBlockVec, &grid);
         if (rc) return rc;
         launch(kern, grid, kThreads, 0, stream, p);
     } else {
-        auto kern = k1::k1_bwd_kernel<T, kThreads, kUnrollBwd, false>;
+        auto kern = k1::k1_bwd_kernel<T, kThreads, kUnrollBwd, false, SCALED>;
         rc = grid_for(kern, dev, p.total, kMinUnitsPerBlockScalar, &grid);
         if (rc) return rc;
         launch(kern, grid, kThreads, 0, stream, p);
@@ -333,6 +335,14 @@ int static_scratch_ptr(int dev, void** out) {
         ptrs[dev] = p;
     }
     *out = ptrs[dev];
+    return K1_OK;
+}
+
+// A logit scale (reciprocal sampling temperature) must be a positive finite number.
+int check_scale(const char* fn, float scale) {
+    if (!(scale > 0.f) || !(scale <= 3.402823466e38f))
+        return fail(K1_ERR_INVALID_ARGUMENT, "%s: scale must be positive and finite (got %g)", fn,
+                    (double)scale);
     return K1_OK;
 }
 
@@ -492,7 +502,8 @@ static int backward_impl(const char* fn, const void* logits, int dtype, int64_t 
                          int64_t outer_stride, int64_t col_offset, const int64_t* targets,
                          const float* lse, const float* entropy, const float* g_logp,
                          const float* g_ent, const float* g_lse, void* d_logits,
-                         int64_t d_inner_stride, int64_t d_outer_stride, void* stream) {
+                         int64_t d_inner_stride, int64_t d_outer_stride, void* stream,
+                         float scale = 1.f) {
     Rows L{n_rows, vocab, inner_rows, inner_stride, outer_stride};
     Rows D{n_rows, vocab, inner_rows, d_inner_stride, d_outer_stride};
     int rc = check_common(fn, logits, dtype, L);
@@ -505,6 +516,22 @@ static int backward_impl(const char* fn, const void* logits, int dtype, int64_t 
     if (reinterpret_cast<uintptr_t>(d_logits) % elem_size(dtype) != 0)
         return fail(K1_ERR_INVALID_ARGUMENT, "%s: d_logits not aligned to its element size", fn);
     cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    if (scale != 1.f) {
+        switch (dtype) {
+            case K1_DTYPE_BF16:
+                return launch_backward<__nv_bfloat16, true>(fn, logits, L, D, col_offset, targets,
+                                                            lse, entropy, g_logp, g_ent, g_lse,
+                                                            d_logits, s, scale);
+            case K1_DTYPE_F16:
+                return launch_backward<__half, true>(fn, logits, L, D, col_offset, targets, lse,
+                                                     entropy, g_logp, g_ent, g_lse, d_logits, s,
+                                                     scale);
+            default:
+                return launch_backward<float, true>(fn, logits, L, D, col_offset, targets, lse,
+                                                    entropy, g_logp, g_ent, g_lse, d_logits, s,
+                                                    scale);
+        }
+    }
     switch (dtype) {
         case K1_DTYPE_BF16:
             return launch_backward<__nv_bfloat16>(fn, logits, L, D, col_offset, targets, lse,
@@ -526,6 +553,55 @@ int k1_fused_logprob_entropy_v1_backward(
     return backward_impl("k1_fused_logprob_entropy_v1_backward", logits, dtype, n_rows, vocab,
                          inner_rows, inner_stride, outer_stride, 0, targets, lse, entropy,
                          g_logp, g_ent, g_lse, d_logits, d_inner_stride, d_outer_stride, stream);
+}
+
+int k1_fused_logprob_entropy_scaled(const void* logits, int dtype, int64_t n_rows,
+                                    int64_t vocab, int64_t inner_rows, int64_t inner_stride,
+                                    int64_t outer_stride, float scale, const int64_t* targets,
+                                    float* logprob, float* entropy, float* lse, void* workspace,
+                                    size_t workspace_bytes, void* stream) {
+    static const char* fn = "k1_fused_logprob_entropy_scaled";
+    Rows L{n_rows, vocab, inner_rows, inner_stride, outer_stride};
+    int rc = check_common(fn, logits, dtype, L);
+    if (rc) return rc;
+    rc = check_scale(fn, scale);
+    if (rc) return rc;
+    if (n_rows == 0) return K1_OK;
+    if (!targets || !logprob || !entropy || !lse)
+        return fail(K1_ERR_INVALID_ARGUMENT, "%s: NULL targets or output pointer", fn);
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    if (scale == 1.f)  // x * 1 rounds to x: the unscaled kernel gives the same bits
+        return k1_fused_logprob_entropy_v1(logits, dtype, n_rows, vocab, inner_rows, inner_stride,
+                                           outer_stride, targets, logprob, entropy, lse,
+                                           workspace, workspace_bytes, stream);
+    switch (dtype) {
+        case K1_DTYPE_BF16:
+            return launch_forward<__nv_bfloat16, false, true>(fn, logits, L, 0, targets, logprob,
+                                                              entropy, lse, nullptr, workspace,
+                                                              workspace_bytes, s, scale);
+        case K1_DTYPE_F16:
+            return launch_forward<__half, false, true>(fn, logits, L, 0, targets, logprob, entropy,
+                                                       lse, nullptr, workspace, workspace_bytes, s,
+                                                       scale);
+        default:
+            return launch_forward<float, false, true>(fn, logits, L, 0, targets, logprob, entropy,
+                                                      lse, nullptr, workspace, workspace_bytes, s,
+                                                      scale);
+    }
+}
+
+int k1_fused_logprob_entropy_scaled_backward(
+    const void* logits, int dtype, int64_t n_rows, int64_t vocab, int64_t inner_rows,
+    int64_t inner_stride, int64_t outer_stride, float scale, const int64_t* targets,
+    const float* lse, const float* entropy, const float* g_logp, const float* g_ent,
+    const float* g_lse, void* d_logits, int64_t d_inner_stride, int64_t d_outer_stride,
+    void* stream) {
+    static const char* fn = "k1_fused_logprob_entropy_scaled_backward";
+    int rc = check_scale(fn, scale);
+    if (rc) return rc;
+    return backward_impl(fn, logits, dtype, n_rows, vocab, inner_rows, inner_stride, outer_stride,
+                         0, targets, lse, entropy, g_logp, g_ent, g_lse, d_logits, d_inner_stride,
+                         d_outer_stride, stream, scale);
 }
 
 int k1_vocab_shard_partials(const void* logits, int dtype, int64_t n_rows, int64_t shard_vocab,

@@ -123,6 +123,13 @@ struct DT<__nv_bfloat16> {
         *p = __float2bfloat16_rn(v);
     }
     __device__ static __forceinline__ float clamp1(float x) { return fmax_nan(x, kLowest); }
+    __device__ static __forceinline__ float round1(float v) {
+        return __bfloat162float(__float2bfloat16_rn(v));
+    }
+    // Both elements of w times s: fp32 products rounded to nearest-even bf16.
+    __device__ static __forceinline__ uint32_t scale2(uint32_t w, float s) {
+        return from_f2(mul2(to_f2(w), splat(s)));
+    }
 };
 
 // d = x - m for the two bf16 logits of w, without a separate conversion: the sm_100
@@ -164,6 +171,11 @@ struct DT<__half> {
     __device__ static __forceinline__ float load1(const __half* p) { return __half2float(*p); }
     __device__ static __forceinline__ void store1(__half* p, float v) { *p = __float2half_rn(v); }
     __device__ static __forceinline__ float clamp1(float x) { return fmax_nan(x, kLowest); }
+    __device__ static __forceinline__ float round1(float v) { return __half2float(__float2half_rn(v)); }
+    // Both elements of w times s: fp32 products rounded to nearest-even fp16.
+    __device__ static __forceinline__ uint32_t scale2(uint32_t w, float s) {
+        return from_f2(mul2(to_f2(w), splat(s)));
+    }
 };
 
 template <>
@@ -174,6 +186,7 @@ struct DT<float> {
     __device__ static __forceinline__ float load1(const float* p) { return *p; }
     __device__ static __forceinline__ void store1(float* p, float v) { *p = v; }
     __device__ static __forceinline__ float clamp1(float x) { return fmax_nan(x, kClampF32); }
+    __device__ static __forceinline__ float round1(float v) { return v; }
 };
 
 // ---------------------------------------------------------------------------------

@@ -42,6 +42,7 @@ struct FwdParams {
     k1_partial* partials;  // shard mode output
     RowPartial* ws_part;   // 2 * gridDim.x slots
     unsigned* ws_ticket;   // gridDim.x counters, zero between calls
+    float scale;           // logits are read as dtype(x * scale); 1 = as stored
 };
 
 struct BwdParams {
@@ -60,7 +61,42 @@ struct BwdParams {
     const float* g_logp;
     const float* g_ent;
     const float* g_lse;
+    float scale;  // logits are read as y = dtype(x * scale), d_logits = dtype(dtype(dL/dy) * scale)
 };
+
+// ---------------------------------------------------------------------------------
+// Scaled logits (sampling temperature).  The scaled entry points read every logit as
+// y = dtype(x * s): the fp32 product rounded to the logits' own type, which is what an
+// in-place `logits.div_(T)` leaves in the tensor (torch divides a tensor by a Python
+// scalar as a multiplication by the fp32 reciprocal s = 1/T).  Their gradient w.r.t. x is
+// dtype(dtype(dL/dy) * s): the rounding of K1's own backward, then the division's
+// backward.  With s = 1 both maps are the identity, so the per-row target-logit loads
+// apply p.scale unconditionally; the per-element paths are compiled with and without it.
+// ---------------------------------------------------------------------------------
+template <typename T>
+__device__ __forceinline__ float scale1(float x, float s) {
+    return DT<T>::round1(__fmul_rn(x, s));
+}
+
+template <typename T>
+__device__ __forceinline__ uint4 scale_vec(uint4 v, float s) {
+    if constexpr (sizeof(T) == 2) {
+        using D = DT<T>;
+        return make_uint4(D::scale2(v.x, s), D::scale2(v.y, s), D::scale2(v.z, s),
+                          D::scale2(v.w, s));
+    } else {
+        const float2 a = mul2(make_float2(__uint_as_float(v.x), __uint_as_float(v.y)), splat(s));
+        const float2 b = mul2(make_float2(__uint_as_float(v.z), __uint_as_float(v.w)), splat(s));
+        return make_uint4(__float_as_uint(a.x), __float_as_uint(a.y), __float_as_uint(b.x),
+                          __float_as_uint(b.y));
+    }
+}
+
+// Target logit of a row as the kernels see it (scaled like every other logit).
+template <typename T>
+__device__ __forceinline__ float target_logit(const T* p, float s) {
+    return scale1<T>(DT<T>::load1(p), s);
+}
 
 // ---------------------------------------------------------------------------------
 // Forward: per-chunk work of one thread
@@ -160,27 +196,43 @@ __device__ __forceinline__ void load_vectors(uint4 (&v)[U], const uint4* vp, int
     for (int u = 0; u < U; ++u) v[u] = ldg_stream(vp + j + (int64_t)u * THREADS);
 }
 
+// Forward chunk load; SCALED applies the logit scale to the loaded vectors.
+template <typename T, bool SCALED, int U, int THREADS>
+__device__ __forceinline__ void load_fwd(uint4 (&v)[U], const uint4* vp, int64_t j, float s) {
+    load_vectors<U, THREADS>(v, vp, j);
+    if constexpr (SCALED) {
+#pragma unroll
+        for (int u = 0; u < U; ++u) v[u] = scale_vec<T>(v[u], s);
+    }
+}
+
 // Predicated chunk load: vectors at or beyond j1 read as padding (the dtype's lowest
 // finite value, which adds exp(-huge) = 0 and is counted like any sub-maximum logit).
-template <typename T, int U, int THREADS>
+// SCALED scales the loaded vectors, never the padding.
+template <typename T, int U, int THREADS, bool SCALED = false>
 __device__ __forceinline__ void load_vectors_masked(uint4 (&v)[U], const uint4* vp, int64_t j,
-                                                    int64_t j1) {
+                                                    int64_t j1, float s = 1.f) {
     const uint32_t pw = DT<T>::kPadWord;
 #pragma unroll
     for (int u = 0; u < U; ++u) {
         const int64_t jj = j + (int64_t)u * THREADS;
-        v[u] = (jj < j1) ? ldg_stream(vp + jj) : make_uint4(pw, pw, pw, pw);
+        if (jj < j1) {
+            v[u] = ldg_stream(vp + jj);
+            if constexpr (SCALED) v[u] = scale_vec<T>(v[u], s);
+        } else {
+            v[u] = make_uint4(pw, pw, pw, pw);
+        }
     }
 }
 
 // The remainder of a segment (fewer than U vectors left for this thread): all its loads
 // are issued at once, then reduced two vectors at a time, so it costs one memory round
 // trip and no arithmetic on padding beyond one vector.
-template <typename T, int THREADS, int U>
+template <typename T, bool SCALED, int THREADS, int U>
 __device__ __forceinline__ void fwd_remainder(const uint4* vp, int64_t j, int64_t j1,
-                                              FwdState& st, bool clamp) {
+                                              FwdState& st, bool clamp, float s) {
     uint4 v[U];
-    load_vectors_masked<T, U, THREADS>(v, vp, j, j1);
+    load_vectors_masked<T, U, THREADS, SCALED>(v, vp, j, j1, s);
 #pragma unroll
     for (int u = 0; u < U; u += 2) {
         if (j + (int64_t)u * THREADS < j1) {
@@ -196,9 +248,9 @@ __device__ __forceinline__ void fwd_remainder(const uint4* vp, int64_t j, int64_
 // while the current chunk is reduced (two register buffers used alternately): warps that
 // start in lock-step (every warp of the grid issues its first loads together) would
 // otherwise alternate between waiting for memory and computing instead of overlapping.
-template <typename T, int THREADS, int U>
+template <typename T, bool SCALED, int THREADS, int U>
 __device__ __forceinline__ void fwd_stream_vec(const T* rowp, int64_t j0, int64_t j1,
-                                               FwdState& st, int tid, bool clamp) {
+                                               FwdState& st, int tid, bool clamp, float s) {
     const uint4* vp = reinterpret_cast<const uint4*>(rowp);
     constexpr int64_t kSpan = (int64_t)(U - 1) * THREADS;
     constexpr int64_t kStep = (int64_t)U * THREADS;
@@ -206,15 +258,15 @@ __device__ __forceinline__ void fwd_stream_vec(const T* rowp, int64_t j0, int64_
     if constexpr (K1_FWD_PREFETCH) {
         if (j + kSpan < j1) {
             uint4 a[U], b[U];
-            load_vectors<U, THREADS>(a, vp, j);
+            load_fwd<T, SCALED, U, THREADS>(a, vp, j, s);
             while (true) {
                 bool more = j + kStep + kSpan < j1;
-                if (more) load_vectors<U, THREADS>(b, vp, j + kStep);
+                if (more) load_fwd<T, SCALED, U, THREADS>(b, vp, j + kStep, s);
                 fwd_chunk<T, U>(a, st, clamp);
                 j += kStep;
                 if (!more) break;
                 more = j + kStep + kSpan < j1;
-                if (more) load_vectors<U, THREADS>(a, vp, j + kStep);
+                if (more) load_fwd<T, SCALED, U, THREADS>(a, vp, j + kStep, s);
                 fwd_chunk<T, U>(b, st, clamp);
                 j += kStep;
                 if (!more) break;
@@ -223,17 +275,17 @@ __device__ __forceinline__ void fwd_stream_vec(const T* rowp, int64_t j0, int64_
     } else {
         for (; j + kSpan < j1; j += kStep) {
             uint4 v[U];
-            load_vectors<U, THREADS>(v, vp, j);
+            load_fwd<T, SCALED, U, THREADS>(v, vp, j, s);
             fwd_chunk<T, U>(v, st, clamp);
         }
     }
-    if (j < j1) fwd_remainder<T, THREADS, U>(vp, j, j1, st, clamp);
+    if (j < j1) fwd_remainder<T, SCALED, THREADS, U>(vp, j, j1, st, clamp, s);
 }
 
 // Stream elements [j0, j1) of one row (scalar path: any alignment).
-template <typename T, int THREADS>
+template <typename T, bool SCALED, int THREADS>
 __device__ __forceinline__ void fwd_stream_scalar(const T* rowp, int64_t j0, int64_t j1,
-                                                  FwdState& st) {
+                                                  FwdState& st, float s) {
     using D = DT<T>;
     constexpr int U = 8;
     for (int64_t j = j0 + threadIdx.x; j < j1; j += (int64_t)U * THREADS) {
@@ -241,7 +293,12 @@ __device__ __forceinline__ void fwd_stream_scalar(const T* rowp, int64_t j0, int
 #pragma unroll
         for (int u = 0; u < U; ++u) {
             int64_t jj = j + (int64_t)u * THREADS;
-            f[u] = (jj < j1) ? D::clamp1(D::load1(rowp + jj)) : D::kLowest;
+            if (jj < j1) {
+                const float x = D::load1(rowp + jj);
+                f[u] = D::clamp1(SCALED ? scale1<T>(x, s) : x);
+            } else {
+                f[u] = D::kLowest;
+            }
         }
         float mx = f[0];
 #pragma unroll
@@ -265,12 +322,12 @@ __device__ __forceinline__ void fwd_emit_row(const FwdParams& p, int64_t r, cons
         out.z = part.z;
         out.t = part.t;
         out.m = part.m;
-        out.x_t = has ? DT<T>::load1(rowp + tl) : 0.f;
+        out.x_t = has ? target_logit<T>(rowp + tl, p.scale) : 0.f;
         out.has_target = has ? 1 : 0;
         out.reserved = 0;
         p.partials[r] = out;
     } else {
-        double xt = (tg >= 0 && tg < p.vocab) ? (double)DT<T>::load1(rowp + tg) : 0.0;
+        double xt = (tg >= 0 && tg < p.vocab) ? (double)target_logit<T>(rowp + tg, p.scale) : 0.0;
         finalize_row(part, xt, p.logprob + r, p.entropy + r, p.lse + r);
     }
 }
@@ -377,7 +434,7 @@ __device__ __forceinline__ void fwd_merge_split_row(const FwdParams& p, int64_t 
         const int64_t tg = p.targets[r];
         const int64_t tl = SHARD ? tg - p.col_offset : tg;
         has = (tg >= 0) && (tl >= 0) && (tl < p.vocab);
-        if (has) xt = DT<T>::load1(rowp + tl);
+        if (has) xt = target_logit<T>(rowp + tl, p.scale);
     }
     __threadfence();
     RowPartial acc;
@@ -425,7 +482,7 @@ __device__ __forceinline__ void fwd_merge_split_row(const FwdParams& p, int64_t 
     }
 }
 
-template <typename T, int THREADS, int U, bool VEC, bool SHARD>
+template <typename T, int THREADS, int U, bool VEC, bool SHARD, bool SCALED = false>
 __global__ void __launch_bounds__(THREADS, K1_FWD_MINB) k1_fwd_kernel(FwdParams p) {
     constexpr int BAR = 0;
     __shared__ FwdSmem<THREADS> sm;
@@ -452,14 +509,14 @@ __global__ void __launch_bounds__(THREADS, K1_FWD_MINB) k1_fwd_kernel(FwdParams 
             // second pass only when the segment holds -inf logits: stream it again, clamped
             for (int pass = 0; pass < 2; ++pass) {
                 st.init();
-                fwd_stream_vec<T, THREADS, U>(rowp, j0, j1, st, tid, pass == 1);
+                fwd_stream_vec<T, SCALED, THREADS, U>(rowp, j0, j1, st, tid, pass == 1, p.scale);
                 if (seg_merge<THREADS, BAR>(st.m, st.z64(), st.t64(), st.m <= DT<T>::kLowest,
                                             pass == 0 && st.saw_neg_inf(), sm, buf, part))
                     break;
             }
         } else {
             st.init();
-            fwd_stream_scalar<T, THREADS>(rowp, j0, j1, st);
+            fwd_stream_scalar<T, SCALED, THREADS>(rowp, j0, j1, st, p.scale);
             seg_merge<THREADS, BAR>(st.m, st.z64(), st.t64(), st.m <= DT<T>::kLowest, false, sm,
                                     buf, part);
         }
@@ -524,9 +581,17 @@ __device__ __forceinline__ float bwd_target_value(float x, const BwdRow& q) {
     return (float)((double)q.gl * om + pt * ((double)q.gs - (double)q.ge * (dt + (double)q.ent)));
 }
 
+// Gradient w.r.t. the stored target logit of row xr: the value above at the scaled logit,
+// rounded to the logits' type, times the scale (both identities at scale 1).
 template <typename T>
-__device__ __forceinline__ uint4 bwd_vector(uint4 v, const BwdRow& q) {
+__device__ __forceinline__ float bwd_target_out(const T* xr, const BwdRow& q, float s) {
+    return scale1<T>(DT<T>::round1(bwd_target_value(target_logit<T>(xr + q.tl, s), q)), s);
+}
+
+template <typename T, bool SCALED = false>
+__device__ __forceinline__ uint4 bwd_vector(uint4 v, const BwdRow& q, float s = 1.f) {
     using D = DT<T>;
+    if constexpr (SCALED) v = scale_vec<T>(v, s);
     const float2 nl = splat(-q.lse), c02 = splat(q.c0), nge = splat(-q.ge);
     uint4 o;
     if constexpr (sizeof(T) == 2) {
@@ -559,6 +624,7 @@ __device__ __forceinline__ uint4 bwd_vector(uint4 v, const BwdRow& q) {
         o = make_uint4(__float_as_uint(out[0]), __float_as_uint(out[1]), __float_as_uint(out[2]),
                        __float_as_uint(out[3]));
     }
+    if constexpr (SCALED) o = scale_vec<T>(o, s);  // o already holds dtype(dL/dy)
     return o;
 }
 
@@ -585,7 +651,7 @@ __device__ __forceinline__ uint4 vec_set(uint4 o, int k, float val) {
     return make_uint4(w[0], w[1], w[2], w[3]);
 }
 
-template <typename T, int THREADS, int U, bool VEC>
+template <typename T, int THREADS, int U, bool VEC, bool SCALED = false>
 __global__ void __launch_bounds__(THREADS, K1_BWD_MINB) k1_bwd_kernel(BwdParams p) {
     using D = DT<T>;
     constexpr int EPV = VEC ? D::kEPV : 1;
@@ -623,10 +689,9 @@ __global__ void __launch_bounds__(THREADS, K1_BWD_MINB) k1_bwd_kernel(BwdParams 
 #pragma unroll
                 for (int u = 0; u < U; ++u) {
                     const int64_t jj = jb + (int64_t)u * THREADS;
-                    uint4 o = bwd_vector<T>(v[u], q);
+                    uint4 o = bwd_vector<T, SCALED>(v[u], q, p.scale);
                     const uint64_t k = (uint64_t)(q.tl - jj * EPV);
-                    if (k < (uint64_t)EPV)
-                        o = vec_set<T>(o, (int)k, bwd_target_value(D::load1(xr + q.tl), q));
+                    if (k < (uint64_t)EPV) o = vec_set<T>(o, (int)k, bwd_target_out<T>(xr, q, p.scale));
                     stg_stream(dv + jj, o);
                 }
             };
@@ -642,27 +707,28 @@ __global__ void __launch_bounds__(THREADS, K1_BWD_MINB) k1_bwd_kernel(BwdParams 
                 for (int u = 0; u < U; ++u) {
                     const int64_t jj = j + (int64_t)u * THREADS;
                     if (jj < j1) {
-                        uint4 o = bwd_vector<T>(v[u], q);
+                        uint4 o = bwd_vector<T, SCALED>(v[u], q, p.scale);
                         const uint64_t k = (uint64_t)(q.tl - jj * EPV);
                         if (k < (uint64_t)EPV)
-                            o = vec_set<T>(o, (int)k, bwd_target_value(D::load1(xr + q.tl), q));
+                            o = vec_set<T>(o, (int)k, bwd_target_out<T>(xr, q, p.scale));
                         stg_stream(dv + jj, o);
                     }
                 }
             }
         } else {
             for (int64_t j = j0 + threadIdx.x; j < j1; j += THREADS) {
-                const float xraw = D::load1(xr + j);
                 float g;
                 if (j == q.tl) {
-                    g = bwd_target_value(xraw, q);
+                    g = bwd_target_out<T>(xr, q, p.scale);
                 } else {
                     // the packed path's operations one lane at a time, so both paths
                     // produce identical bits
-                    const float x = D::clamp1(xraw);
+                    const float xraw = D::load1(xr + j);
+                    const float x = D::clamp1(SCALED ? scale1<T>(xraw, p.scale) : xraw);
                     const float d = __fadd_rn(x, -q.lse);
                     const float pp = ex2(__fmul_rn(d, kLog2e));
                     g = __fmaf_rn(-q.ge, __fmul_rn(pp, d), __fmul_rn(pp, q.c0));
+                    if constexpr (SCALED) g = scale1<T>(D::round1(g), p.scale);
                 }
                 D::store1(dr + j, g);
             }

@@ -194,7 +194,7 @@ __global__ void __launch_bounds__((NCW + 1) * 32, K1_RING_FWD_MINB) k1_fwd_ring_
                                 st.saw_neg_inf(), sm, buf, part)) {
             // rare: the segment holds -inf logits; stream it again from global, clamped
             st.init();
-            fwd_stream_vec<T, NC, 4>(rowp, j0, j1, st, tid, true);
+            fwd_stream_vec<T, false, NC, 4>(rowp, j0, j1, st, tid, true, 1.f);
             seg_merge<NC, BAR>(st.m, st.z64(), st.t64(), st.m <= DT<T>::kLowest, false, sm, buf,
                                part);
         }
@@ -236,7 +236,7 @@ __global__ void __launch_bounds__((NCW + 1) * 32, K1_RING_FWD_MINB) k1_fwd_ring_
     }
 }
 
-template <typename T, int NCW, int STAGES, int SBYTES>
+template <typename T, int NCW, int STAGES, int SBYTES, bool SCALED = false>
 __global__ void __launch_bounds__((NCW + 1) * 32, K1_RING_MINB) k1_bwd_ring_kernel(BwdParams p) {
     using D = DT<T>;
     constexpr int NC = NCW * 32;
@@ -298,10 +298,10 @@ __global__ void __launch_bounds__((NCW + 1) * 32, K1_RING_MINB) k1_bwd_ring_kern
                     const int64_t i = tid + u * NC;
                     if (i < n) {
                         const int64_t jv = jj + i;
-                        uint4 o = bwd_vector<T>(stage[i], q);
+                        uint4 o = bwd_vector<T, SCALED>(stage[i], q, p.scale);
                         const uint64_t kk = (uint64_t)(q.tl - jv * EPV);
                         if (kk < (uint64_t)EPV)
-                            o = vec_set<T>(o, (int)kk, bwd_target_value(D::load1(xr + q.tl), q));
+                            o = vec_set<T>(o, (int)kk, bwd_target_out<T>(xr, q, p.scale));
                         stg_stream(dv + jv, o);
                     }
                 }

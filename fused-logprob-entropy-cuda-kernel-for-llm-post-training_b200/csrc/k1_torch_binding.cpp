@@ -155,6 +155,26 @@ void fused_logprob_entropy_v1(at::Tensor logits, at::Tensor targets, at::Tensor 
         lse_out.data_ptr<float>(), ws, ws_bytes, at::cuda::getCurrentCUDAStream().stream()));
 }
 
+// _C.fused_logprob_entropy_scaled: the forward on logits read as dtype(x * scale) (the
+// GRPO temperature, scale = 1/T in fp32), in place of `logits.div_(T)` + K1 (reference
+// python/kernel_opt/trainer.py:101-127).
+void fused_logprob_entropy_scaled(at::Tensor logits, at::Tensor targets, at::Tensor logprob,
+                                  at::Tensor entropy, at::Tensor lse_out, double scale) {
+    const int dt = dtype_code(logits);
+    TORCH_CHECK(dt >= 0, "logits dtype must be bf16, fp16, or fp32");
+    Rows L = logits_rows(logits);
+    check_fwd_common(logits, targets, logprob, entropy, lse_out, L.n_rows);
+    if (L.n_rows == 0) return;
+    c10::cuda::CUDAGuard guard(logits.device());
+    size_t ws_bytes = 0;
+    void* ws = forward_workspace(logits, &ws_bytes);
+    check_rc(k1_fused_logprob_entropy_scaled(
+        logits.data_ptr(), dt, L.n_rows, L.vocab, L.inner_rows, L.inner_stride, L.outer_stride,
+        (float)scale, targets.data_ptr<int64_t>(), logprob.data_ptr<float>(),
+        entropy.data_ptr<float>(), lse_out.data_ptr<float>(), ws, ws_bytes,
+        at::cuda::getCurrentCUDAStream().stream()));
+}
+
 // _C.fused_logprob_entropy_naive (reference csrc/fused_logprob.cu:405-458)
 void fused_logprob_entropy_naive(at::Tensor logits, at::Tensor targets, at::Tensor logprob,
                                  at::Tensor entropy, at::Tensor lse_out) {
@@ -183,7 +203,7 @@ const float* opt_grad(const c10::optional<at::Tensor>& g, int64_t n_rows, const 
 void backward_common(const char* which, at::Tensor logits, at::Tensor targets, int64_t vocab_offset,
                      at::Tensor lse, at::Tensor entropy, c10::optional<at::Tensor> g_logp,
                      c10::optional<at::Tensor> g_ent, c10::optional<at::Tensor> g_lse,
-                     at::Tensor d_logits) {
+                     at::Tensor d_logits, double scale = 1.0) {
     TORCH_CHECK(logits.is_cuda(), "logits must be contiguous CUDA");
     TORCH_CHECK(targets.scalar_type() == at::kLong, "targets must be int64");
     TORCH_CHECK(targets.is_contiguous() && targets.is_cuda(), "targets must be contiguous CUDA");
@@ -234,6 +254,12 @@ void backward_common(const char* which, at::Tensor logits, at::Tensor targets, i
                                      targets.data_ptr<int64_t>(), lse.data_ptr<float>(),
                                      entropy.data_ptr<float>(), gl, ge, gs, d_logits.data_ptr(),
                                      D.inner_stride, D.outer_stride, s);
+    } else if (which[0] == 's') {
+        rc = k1_fused_logprob_entropy_scaled_backward(
+            logits.data_ptr(), dt, L.n_rows, L.vocab, L.inner_rows, L.inner_stride, L.outer_stride,
+            (float)scale, targets.data_ptr<int64_t>(), lse.data_ptr<float>(),
+            entropy.data_ptr<float>(), gl, ge, gs, d_logits.data_ptr(), D.inner_stride,
+            D.outer_stride, s);
     } else {
         rc = k1_fused_logprob_entropy_v1_backward(
             logits.data_ptr(), dt, L.n_rows, L.vocab, L.inner_rows, L.inner_stride, L.outer_stride,
@@ -249,6 +275,16 @@ void fused_logprob_entropy_v1_backward(at::Tensor logits, at::Tensor targets, at
                                        c10::optional<at::Tensor> g_ent,
                                        c10::optional<at::Tensor> g_lse, at::Tensor d_logits) {
     backward_common("b", logits, targets, 0, lse, entropy, g_logp, g_ent, g_lse, d_logits);
+}
+
+// _C.fused_logprob_entropy_scaled_backward: gradient w.r.t. the unscaled logits x,
+// dtype(dtype(dL/dy) * scale) with y = dtype(x * scale).
+void fused_logprob_entropy_scaled_backward(at::Tensor logits, at::Tensor targets, at::Tensor lse,
+                                           at::Tensor entropy, c10::optional<at::Tensor> g_logp,
+                                           c10::optional<at::Tensor> g_ent,
+                                           c10::optional<at::Tensor> g_lse, at::Tensor d_logits,
+                                           double scale) {
+    backward_common("s", logits, targets, 0, lse, entropy, g_logp, g_ent, g_lse, d_logits, scale);
 }
 
 // Vocab-parallel step 1: partials [n_rows, 4] float64 (one k1_partial per row).
@@ -322,6 +358,15 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
           pybind11::arg("targets"), pybind11::arg("lse"), pybind11::arg("entropy"),
           pybind11::arg("g_logp"), pybind11::arg("g_ent"), pybind11::arg("g_lse"),
           pybind11::arg("d_logits"));
+    m.def("fused_logprob_entropy_scaled", &fused_logprob_entropy_scaled,
+          "Forward on logits read as dtype(x * scale) (temperature folded in).",
+          pybind11::arg("logits"), pybind11::arg("targets"), pybind11::arg("logprob"),
+          pybind11::arg("entropy"), pybind11::arg("lse_out"), pybind11::arg("scale"));
+    m.def("fused_logprob_entropy_scaled_backward", &fused_logprob_entropy_scaled_backward,
+          "Backward of the scaled forward, gradient w.r.t. the unscaled logits.",
+          pybind11::arg("logits"), pybind11::arg("targets"), pybind11::arg("lse"),
+          pybind11::arg("entropy"), pybind11::arg("g_logp"), pybind11::arg("g_ent"),
+          pybind11::arg("g_lse"), pybind11::arg("d_logits"), pybind11::arg("scale"));
     m.def("vocab_shard_partials", &vocab_shard_partials,
           "Vocab-parallel: per-row partial state of a vocabulary shard.");
     m.def("vocab_combine", &vocab_combine, "Vocab-parallel: merge gathered shard partials.");

@@ -3,8 +3,14 @@
 Same override as the reference (python/kernel_opt/trainer.py:1-131): only
 `_get_per_token_logps_and_entropies` changes, which is TRL's single entry point for the
 policy, old-policy and reference log-prob computations.  Multimodal inputs fall back to
-the parent.  Unlike the reference, the completion window of each chunk is one K1 launch
-on the strided [B, L', V] view instead of a loop over batch elements.
+the parent.  Unlike the reference, each chunk is one K1 launch on the strided [B, L', V]
+completion window instead of a loop over batch elements, the temperature is applied
+inside the kernels instead of by an in-place division, and the backward writes the
+parent-shaped logits gradient directly (`grpo.window_logps_and_entropies`).  Results are
+bit-identical to the reference's slice + `div_` + K1 sequence.
+
+`k1_inplace_backward=True` (constructor keyword) lets the backward overwrite the model's
+logits with their gradient, which removes the second [B, L, V] buffer of the loss block.
 
 Requires `trl` (imported at module load, as in the reference); `kernel_opt` imports
 this module lazily.
@@ -14,11 +20,15 @@ from __future__ import annotations
 import torch
 from trl import GRPOTrainer
 
-from .grpo import MULTIMODAL_KWARGS, completion_window, k1_logps_and_entropies
+from .grpo import MULTIMODAL_KWARGS, window_logps_and_entropies
 
 
 class KernelOptGRPOTrainer(GRPOTrainer):
     """trl.GRPOTrainer with the inner logprob+entropy block replaced by K1."""
+
+    def __init__(self, *args, k1_inplace_backward: bool = False, **kwargs):
+        super().__init__(*args, **kwargs)
+        self.k1_inplace_backward = k1_inplace_backward
 
     def _get_per_token_logps_and_entropies(
         self,
@@ -63,10 +73,11 @@ class KernelOptGRPOTrainer(GRPOTrainer):
             model_inputs["use_cache"] = False
 
             logits = model(**model_inputs).logits
-            logits = completion_window(logits, logits_to_keep)
-            logits.div_(self.temperature)  # in place, as TRL does
             completion_ids = input_ids_batch[:, -logits_to_keep:]
-            logps, ents = k1_logps_and_entropies(logits, completion_ids, compute_entropy)
+            # completion window, temperature and K1 in one launch each way
+            logps, ents = window_logps_and_entropies(
+                logits, completion_ids, logits_to_keep, self.temperature, compute_entropy,
+                inplace_backward=getattr(self, "k1_inplace_backward", False) and torch.is_grad_enabled())
             all_logps.append(logps)
             if compute_entropy:
                 all_entropies.append(ents)

@@ -39,7 +39,8 @@
 extern "C" {
 #endif
 
-#define K1_ABI_VERSION 1
+/* 1: initial entry points; 2: adds the scaled forward and backward. */
+#define K1_ABI_VERSION 2
 
 /* Element type of logits and d_logits.  Outputs and saved rows are always fp32. */
 typedef enum k1_dtype {
@@ -158,6 +159,34 @@ int k1_fused_logprob_entropy_v1_backward(
     int64_t inner_stride, int64_t outer_stride, const int64_t* targets, const float* lse,
     const float* entropy, const float* g_logp, const float* g_ent, const float* g_lse,
     void* d_logits, int64_t d_inner_stride, int64_t d_outer_stride, void* stream);
+
+/*
+ * Forward and backward with the logits scaled on the fly (the GRPO sampling temperature),
+ * for the reference trainer's `logits.div_(self.temperature)` followed by K1 on the
+ * completion window (reference python/kernel_opt/trainer.py:101-127).  Every logit x is read
+ * as y = dtype(x * scale): the fp32 product rounded to nearest-even in the logits' type, which
+ * is the tensor torch's in-place division leaves behind (torch divides by a Python scalar T
+ * as a multiplication by the fp32 reciprocal, so pass scale = 1.0f / (float)T).  The forward
+ * results are those of k1_fused_logprob_entropy_v1 on y, bit for bit; the backward writes the
+ * gradient with respect to x, d_logits = dtype(dtype(dL/dy) * scale): K1's backward on y
+ * followed by the division's own backward, again bit for bit.  The division pass, its
+ * backward pass and the temporary that holds y are gone.  scale must be positive and finite;
+ * scale == 1 runs the unscaled kernels.  All other arguments as for
+ * k1_fused_logprob_entropy_v1 / _v1_backward (d_logits may alias logits: in place).
+ * No single counterpart in the reference.
+ */
+int k1_fused_logprob_entropy_scaled(const void* logits, int dtype, int64_t n_rows,
+                                    int64_t vocab, int64_t inner_rows, int64_t inner_stride,
+                                    int64_t outer_stride, float scale, const int64_t* targets,
+                                    float* logprob, float* entropy, float* lse, void* workspace,
+                                    size_t workspace_bytes, void* stream);
+
+int k1_fused_logprob_entropy_scaled_backward(
+    const void* logits, int dtype, int64_t n_rows, int64_t vocab, int64_t inner_rows,
+    int64_t inner_stride, int64_t outer_stride, float scale, const int64_t* targets,
+    const float* lse, const float* entropy, const float* g_logp, const float* g_ent,
+    const float* g_lse, void* d_logits, int64_t d_inner_stride, int64_t d_outer_stride,
+    void* stream);
 
 /*
  * Vocab-parallel forward, step 1 of 3: per-row partial state of this rank's vocabulary

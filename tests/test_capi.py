@@ -30,7 +30,7 @@ def test_every_declared_symbol_is_exported(lib):
 
 def test_abi_version(lib):
     lib.k1_abi_version.restype = ctypes.c_int
-    assert lib.k1_abi_version() == 1
+    assert lib.k1_abi_version() == 2
 
 
 def _fwd(lib, dtype=2, n_rows=4, vocab=16, inner_rows=4, inner_stride=16, outer=0,
@@ -91,3 +91,26 @@ def test_backward_and_combine_validation(lib):
     v.argtypes = [p, c_int, i64, i64, i64, i64, i64, i64, p, p, p, ctypes.c_size_t, p]
     v.restype = c_int
     assert v(1024, 2, 4, 16, 4, 16, 0, -5, 2048, 4096, 8192, 1 << 20, None) == K1_ERR_INVALID
+
+
+def test_scaled_entry_points_validate_scale(lib):
+    """The scaled forward / backward reject a scale that is not positive and finite
+    before any device call (so this runs without a GPU)."""
+    i64, p, c_int, c_float = ctypes.c_int64, ctypes.c_void_p, ctypes.c_int, ctypes.c_float
+    f = lib.k1_fused_logprob_entropy_scaled
+    f.argtypes = [p, c_int, i64, i64, i64, i64, i64, c_float, p, p, p, p, p, ctypes.c_size_t, p]
+    f.restype = c_int
+    b = lib.k1_fused_logprob_entropy_scaled_backward
+    b.argtypes = [p, c_int, i64, i64, i64, i64, i64, c_float, p, p, p, p, p, p, p, i64, i64, p]
+    b.restype = c_int
+    for s in (0.0, -0.5, float("inf"), float("nan")):
+        assert f(1024, 2, 4, 16, 4, 16, 0, s, 2048, 4096, 4096, 4096, 8192, 1 << 20,
+                 None) == K1_ERR_INVALID
+        assert "scale" in _err(lib)
+        assert b(1024, 2, 4, 16, 4, 16, 0, s, 2048, 4096, 4096, None, None, None, 8192, 16, 0,
+                 None) == K1_ERR_INVALID
+        assert "scale" in _err(lib)
+    # dtype is still checked first, and zero rows are a no-op
+    assert f(1024, 7, 4, 16, 4, 16, 0, 1.5, 2048, 4096, 4096, 4096, 8192, 1 << 20,
+             None) == K1_ERR_DTYPE
+    assert f(0, 2, 0, 16, 1, 16, 0, 1.5, 0, 0, 0, 0, 0, 0, None) == K1_OK

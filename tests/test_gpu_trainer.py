@@ -57,9 +57,10 @@ def _eager(model, input_ids, attention_mask, logits_to_keep, temperature):
 
 
 @pytest.mark.parametrize("batch_size", [None, 2])
-def test_override_matches_eager_and_backprops(trainer_cls, batch_size):
+@pytest.mark.parametrize("inplace", [False, True])
+def test_override_matches_eager_and_backprops(trainer_cls, batch_size, inplace):
     model = _TinyLM().cuda()
-    tr = trainer_cls()
+    tr = trainer_cls(k1_inplace_backward=inplace)
     tr.temperature = 0.7
     tr.model_kwarg_keys = {"input_ids", "attention_mask", "logits_to_keep", "use_cache"}
     g = torch.Generator().manual_seed(1)
@@ -79,6 +80,43 @@ def test_override_matches_eager_and_backprops(trainer_cls, batch_size):
     model.zero_grad()
     ref_lp.sum().backward()
     torch.testing.assert_close(grad_ours, model.head.grad, rtol=2e-2, atol=2e-3)
+
+
+def test_override_equals_reference_sequence_bitwise(trainer_cls):
+    """The override's logps and the logits gradient equal what the reference's own
+    sequence (slice, in-place div_ by the temperature, K1) gives with our K1, bit for bit."""
+    import kernel_opt
+    from kernel_opt import grpo
+
+    model = _TinyLM().cuda()
+    tr = trainer_cls()
+    tr.temperature = 0.9
+    tr.model_kwarg_keys = {"input_ids", "attention_mask", "logits_to_keep", "use_cache"}
+    input_ids = torch.randint(0, 3000, (4, 30), generator=torch.Generator().manual_seed(3)).cuda()
+    K = 12
+    captured = {}
+    fwd = model.forward
+
+    def spy(*a, **k):
+        out = fwd(*a, **k)
+        out.logits.retain_grad()
+        captured["logits"] = out.logits
+        return out
+
+    model.forward = spy
+    logps, _ = tr._get_per_token_logps_and_entropies(model, input_ids, torch.ones_like(input_ids), K)
+    logps.sum().backward()
+    g_ours = captured["logits"].grad.clone()
+
+    x0 = fwd(input_ids, None, logits_to_keep=K + 1).logits
+    x0.retain_grad()
+    logits = x0 * 1  # the in-place division below must not touch x0 (its .grad is compared)
+    w = grpo.completion_window(logits, K)
+    w.div_(tr.temperature)
+    ref, _, _ = kernel_opt.fused_logprob_entropy(w, input_ids[:, -K:].contiguous())
+    ref.sum().backward()
+    torch.testing.assert_close(logps.detach(), ref.detach(), rtol=0, atol=0)
+    torch.testing.assert_close(g_ours, x0.grad, rtol=0, atol=0)
 
 
 def test_multimodal_falls_back_to_parent(trainer_cls):

@@ -1,5 +1,8 @@
 """kernel_opt imports without a GPU (its native extension and C-ABI library load), keeps
 the reference's public surface, and reports bad input the way the reference does."""
+import os
+
+import numpy as np
 import pytest
 import torch
 
@@ -15,7 +18,7 @@ def test_public_surface_matches_reference():
     for name in ("fused_logprob_entropy_naive", "fused_logprob_entropy_v1",
                  "fused_logprob_entropy_v1_backward"):
         assert callable(getattr(_C, name))
-    assert _C.abi_version() == 1
+    assert _C.abi_version() == 2
 
 
 def test_trainer_is_lazy():
@@ -26,7 +29,6 @@ def test_trainer_is_lazy():
 
 
 def test_native_libraries_are_the_in_tree_builds():
-    import os
     maps = open("/proc/self/maps").read()
     root = os.path.dirname(kernel_opt.__file__)
     assert os.path.join(root, "lib", "libk1_b200.so") in maps
@@ -68,6 +70,15 @@ def test_completion_window_is_a_strided_view():
     torch.testing.assert_close(w, base[:, :-1][:, -6:])
 
 
+def test_temperature_scale_is_the_fp32_reciprocal():
+    for T in (0.7, 0.9, 1.3, 2.0, 1e-3, 1.0):
+        assert grpo.temperature_scale(T) == float(np.float32(1.0) / np.float32(T))
+    assert grpo.temperature_scale(1.0) == 1.0
+    for bad in (0.0, -1.0, float("inf"), float("nan")):
+        with pytest.raises(ValueError):
+            grpo.temperature_scale(bad)
+
+
 def test_custom_op_fake_shapes():
     """The registered op's fake implementation (used by torch.compile tracing)."""
     from kernel_opt import ops
@@ -78,3 +89,17 @@ def test_custom_op_fake_shapes():
     d = ops._bwd_op(x, t, l, h, lp, None, None)
     assert d.shape == x.shape and d.dtype == x.dtype
     assert hasattr(torch.ops.kernel_opt, "fused_logprob_entropy_fwd")
+
+
+def test_binding_exports_every_function_the_package_calls():
+    """Every `_C.<name>` used by the Python layer exists in the built extension (a stale
+    build fails here, not on the GPU box)."""
+    import re
+    pkg = os.path.dirname(kernel_opt.__file__)
+    used = set()
+    for f in os.listdir(pkg):
+        if f.endswith(".py"):
+            used |= set(re.findall(r"\b_C\.(\w+)", open(os.path.join(pkg, f)).read()))
+    assert used, "no _C calls found"
+    missing = sorted(n for n in used if not hasattr(_C, n))
+    assert not missing, f"kernel_opt._C lacks {missing}; rebuild the extension"
