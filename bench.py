@@ -627,6 +627,142 @@ def grpo_arm(args, cfg, rank, local_rank, world):
     print(json.dumps(out), flush=True)
 
 
+def lmhead_arm(args, cfg, rank, local_rank, world):
+    """LM head fused with K1 (kernel_opt.lm_head) against materialised logits, on config 3's
+    rows and vocabulary with a Qwen2.5-7B-sized hidden state (H = 3584), bf16:
+      fused        -- GEMM in L2-sized row chunks, K1 on each chunk from L2; backward
+                      recomputes each chunk's logits (4 GEMMs per step);
+      materialised -- logits = h W^T ([N, V] in HBM), K1 with the temperature folded in,
+                      autograd (3 GEMMs per step).
+    Both: forward + backward to hidden and weight, and a no-grad forward (the old-policy /
+    reference-policy log-probs of GRPO).  Peak extra device memory of each."""
+    import torch.distributed as dist
+
+    import kernel_opt
+    from kernel_opt import lm_head
+
+    device = torch.device("cuda", local_rank)
+    torch.cuda.set_device(device)
+    if world > 1:
+        dist.init_process_group("nccl", rank=rank, world_size=world, device_id=device,
+                                timeout=datetime.timedelta(seconds=300))
+    B, S, V, H = 16, 1024, 151936, 3584
+    N = B * S
+    dt = torch.bfloat16
+    T = 0.7
+    gen = torch.Generator(device=device).manual_seed(99 + rank)
+    h = (torch.randn(N, H, generator=gen, device=device) * 0.5).to(dt)
+    w = (torch.randn(V, H, generator=gen, device=device) * (2.5 / H ** 0.5)).to(dt)
+    t = torch.randint(0, V, (N,), generator=gen, device=device)
+    g_lp = torch.full((N,), -1.0 / N, device=device)
+    g_h = torch.full((N,), -0.01 / N, device=device)
+    stream = torch.cuda.current_stream(device)
+    gemm_flops = 2.0 * N * H * V
+
+    chunk_default = lm_head.default_chunk_rows(N, V, 2)
+    chunk = [chunk_default]
+
+    def fused_step(grad):
+        hx = h.detach().requires_grad_(grad)
+        wx = w.detach().requires_grad_(grad)
+        lp, ent, _ = lm_head.fused_linear_logprob_entropy(hx, wx, t, T, chunk_rows=chunk[0])
+        if grad:
+            torch.autograd.grad((lp, ent), (hx, wx), (g_lp, g_h))
+
+    def materialised_step(grad):
+        hx = h.detach().requires_grad_(grad)
+        wx = w.detach().requires_grad_(grad)
+        z = hx @ wx.t()
+        lp, ent, _ = kernel_opt.fused_logprob_entropy_scaled(z, t, T)
+        if grad:
+            torch.autograd.grad((lp, ent), (hx, wx), (g_lp, g_h))
+
+    def timed(fn, grad, K):
+        for _ in range(max(3, args.warmup)):
+            fn(grad)
+        torch.cuda.synchronize(device)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        for _ in range(K):
+            with torch.set_grad_enabled(grad):
+                fn(grad)
+        b.record(stream)
+        torch.cuda.synchronize(device)
+        return a.elapsed_time(b) / K
+
+    def peak_extra(fn, grad):
+        torch.cuda.synchronize(device)
+        torch.cuda.reset_peak_memory_stats(device)
+        base = torch.cuda.memory_allocated(device)
+        with torch.set_grad_enabled(grad):
+            fn(grad)
+        torch.cuda.synchronize(device)
+        return torch.cuda.max_memory_allocated(device) - base
+
+    K = max(1, min(args.steps, 10))
+    with ClockSampler(device) as clocks:
+        if world > 1:
+            dist.barrier(device_ids=[local_rank])
+        fused_ms = timed(fused_step, True, K)
+    res = {
+        "fused_train_ms": fused_ms,
+        "materialised_train_ms": timed(materialised_step, True, K),
+        "fused_nograd_ms": timed(fused_step, False, K),
+        "materialised_nograd_ms": timed(materialised_step, False, K),
+    }
+    mem = {"fused_train": peak_extra(fused_step, True),
+           "materialised_train": peak_extra(materialised_step, True),
+           "fused_nograd": peak_extra(fused_step, False),
+           "materialised_nograd": peak_extra(materialised_step, False)}
+    sweep = []
+    for c in (256, 1024, 2048, 4096, 8192):
+        chunk[0] = c
+        sweep.append({"chunk_rows": c, "train_ms": round(timed(fused_step, True, 2), 3),
+                      "nograd_ms": round(timed(fused_step, False, 2), 3),
+                      "train_peak_extra_bytes": peak_extra(fused_step, True)})
+    chunk[0] = chunk_default
+    tt = torch.tensor([fused_ms], device=device, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        dist.barrier(device_ids=[local_rank])
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    max_ms = float(tt.item())
+    peaks = {}
+    try:
+        with open(os.path.join(REPO, "MEASURED_PEAKS.json")) as f:
+            peaks = json.load(f)
+    except Exception:
+        pass
+    tc_peak = float(peaks.get("bf16_tflops_sustained") or peaks.get("bf16_tflops") or 1400.0)
+    useful = 3 * gemm_flops  # forward logits, dh, dW
+    out = {
+        "metric": "LM head + K1 fwd+bwd, useful GEMM TFLOP/s (3 GEMMs per step)",
+        "value": round(useful * world / (max_ms / 1e3) / 1e12, 1), "unit": "TFLOP/s",
+        "n_gpus": world, "steps": K, "warmup": max(3, args.warmup), "ms_per_step": round(max_ms, 3),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic",
+        "config": {"workload": "LM head [3584 -> 151936] + K1 on config 3's 16 x 1024 rows",
+                   "rows": N, "hidden": H, "vocab": V, "temperature": T,
+                   "chunk_rows": chunk_default,
+                   "parallelism": f"row-sharded x{world} (no collective)"},
+        "times_ms": {k: round(v, 3) for k, v in res.items()},
+        "speedup_train": round(res["materialised_train_ms"] / res["fused_train_ms"], 3),
+        "speedup_nograd": round(res["materialised_nograd_ms"] / res["fused_nograd_ms"], 3),
+        "peak_extra_bytes": mem,
+        "chunk_sweep": sweep,
+        "roofline": {"bound": "tensor", "achieved": round(4 * gemm_flops / (max_ms / 1e3) / 1e12, 1),
+                     "peak": tc_peak, "unit": "TFLOP/s",
+                     "frac": round(4 * gemm_flops / (max_ms / 1e3) / 1e12 / tc_peak, 4),
+                     "note": "4 GEMMs executed per fused step (incl. the recomputation), "
+                             "library GEMMs; peak = MEASURED_PEAKS.json bf16 sustained"},
+        "gpu_launches": 2 * -(-N // chunk_default) * K,
+        "clocks": clocks.summary(),
+    }
+    print(json.dumps(out), flush=True)
+
+
 def vocab_arm(args, cfg, rank, local_rank, world):
     """Vocab-parallel K1 (tensor-parallel LM head layout): rank k holds columns
     vocab_shard(V, world, k) of every row; forward = shard partials + one all-gather + merge,
@@ -712,9 +848,10 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--config", choices=sorted(CONFIGS), default="c2")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--mode", choices=["rows", "vocab", "grpo"], default="rows",
+    ap.add_argument("--mode", choices=["rows", "vocab", "grpo", "lmhead"], default="rows",
                     help="rows: row-sharded (default); vocab: vocab-parallel (config c5); "
-                         "grpo: the GRPO loss block on config c3, fused vs unfused")
+                         "grpo: the GRPO loss block on config c3, fused vs unfused; "
+                         "lmhead: LM head fused with K1 vs materialised logits")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -724,6 +861,8 @@ def main():
         reference_arm(args, cfg, rank, world)
     elif args.mode == "grpo":
         grpo_arm(args, cfg, rank, local_rank, world)
+    elif args.mode == "lmhead":
+        lmhead_arm(args, cfg, rank, local_rank, world)
     elif args.mode == "vocab":
         vocab_arm(args, CONFIGS["c5"] if args.config == "c2" else cfg, rank, local_rank, world)
     else:

@@ -3,7 +3,9 @@ over [..., V] logits, forward and backward, in one streaming pass each.
 
 Drop-in for the reference package of the same name (python/kernel_opt/__init__.py:1-15):
 the same public functions, the same `_C` binding names, and the lazily imported
-`KernelOptGRPOTrainer` (needs `trl`).  Multi-GPU helpers live in `kernel_opt.parallel`.
+`KernelOptGRPOTrainer` (needs `trl`).  Multi-GPU helpers live in `kernel_opt.parallel`,
+the GRPO completion-window node in `kernel_opt.grpo`, the LM head fused with K1 in
+`kernel_opt.lm_head`.
 """
 import torch  # noqa: F401  (loads libc10 / libtorch before the extension)
 
@@ -18,7 +20,9 @@ from .ops import (  # noqa: F401
     fused_logprob_entropy,
     fused_logprob_entropy_forward,
     fused_logprob_entropy_naive,
+    fused_logprob_entropy_scaled,
 )
+from .lm_head import fused_linear_logprob_entropy  # noqa: F401
 
 
 def __getattr__(name):

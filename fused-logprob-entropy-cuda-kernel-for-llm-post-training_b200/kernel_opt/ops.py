@@ -89,6 +89,45 @@ class _FusedLogprobEntropy(torch.autograd.Function):
         return d_logits, None
 
 
+class _FusedLogprobEntropyScaled(torch.autograd.Function):
+    """K1 on logits divided by a temperature, the division done inside the kernels with
+    the rounding of `logits.div_(T)` (see k1_fused_logprob_entropy_scaled)."""
+
+    @staticmethod
+    def forward(ctx, logits, targets, scale):
+        _check_inputs(logits, targets)
+        targets = targets.contiguous()
+        logprob, entropy, lse = _alloc_outputs(targets)
+        _C.fused_logprob_entropy_scaled(logits, targets, logprob, entropy, lse, scale)
+        ctx.save_for_backward(logits, targets, lse, entropy)
+        ctx.scale = scale
+        ctx.set_materialize_grads(False)
+        return logprob, entropy, lse
+
+    @staticmethod
+    def backward(ctx, g_logp, g_ent, g_lse):
+        logits, targets, lse, entropy = ctx.saved_tensors
+
+        def _prep(g):
+            return None if g is None else g.to(torch.float32, copy=False).contiguous()
+
+        d_logits = torch.empty_like(logits)
+        _C.fused_logprob_entropy_scaled_backward(
+            logits, targets, lse, entropy, _prep(g_logp), _prep(g_ent), _prep(g_lse), d_logits,
+            ctx.scale)
+        return d_logits, None, None
+
+
+def fused_logprob_entropy_scaled(logits: torch.Tensor, targets: torch.Tensor,
+                                 temperature: float = 1.0):
+    """`fused_logprob_entropy(logits / temperature, targets)` without the division pass:
+    same results and gradient (w.r.t. the undivided logits) bit for bit, one launch each
+    way.  No counterpart in the reference, whose trainer divides in place first
+    (python/kernel_opt/trainer.py:101)."""
+    from .grpo import temperature_scale
+    return _FusedLogprobEntropyScaled.apply(logits, targets, temperature_scale(temperature))
+
+
 # ---------------------------------------------------------------------------------------
 # torch.library registration: under torch.compile K1 is one opaque op with a fake (meta)
 # implementation and an autograd formula, so compiled graphs contain it without a graph

@@ -12,23 +12,35 @@ bit-identical to the reference's slice + `div_` + K1 sequence.
 `k1_inplace_backward=True` (constructor keyword) lets the backward overwrite the model's
 logits with their gradient, which removes the second [B, L, V] buffer of the loss block.
 
+`k1_fused_lm_head=True` (constructor keyword) skips the logits tensor altogether: the
+decoder's last hidden state of the completion window goes through
+`kernel_opt.lm_head.fused_linear_logprob_entropy` (LM-head GEMM in L2-sized row chunks, K1
+on each chunk).  Only for models whose head is a plain bias-free linear map of the final
+hidden state; other models (logit soft-capping or scaling, a head bias) keep the standard
+path, with a warning.
+
 Requires `trl` (imported at module load, as in the reference); `kernel_opt` imports
 this module lazily.
 """
 from __future__ import annotations
 
+import warnings
+
 import torch
 from trl import GRPOTrainer
 
 from .grpo import MULTIMODAL_KWARGS, window_logps_and_entropies
+from .lm_head import fused_head_parts, fused_linear_logprob_entropy
 
 
 class KernelOptGRPOTrainer(GRPOTrainer):
     """trl.GRPOTrainer with the inner logprob+entropy block replaced by K1."""
 
-    def __init__(self, *args, k1_inplace_backward: bool = False, **kwargs):
+    def __init__(self, *args, k1_inplace_backward: bool = False, k1_fused_lm_head: bool = False,
+                 **kwargs):
         super().__init__(*args, **kwargs)
         self.k1_inplace_backward = k1_inplace_backward
+        self.k1_fused_lm_head = k1_fused_lm_head
 
     def _get_per_token_logps_and_entropies(
         self,
@@ -59,12 +71,31 @@ class KernelOptGRPOTrainer(GRPOTrainer):
                 model, input_ids, attention_mask, logits_to_keep,
                 batch_size=batch_size, compute_entropy=compute_entropy, **extra)
 
+        parts = None
+        if getattr(self, "k1_fused_lm_head", False):
+            parts = fused_head_parts(model)
+            if parts is None:
+                warnings.warn("k1_fused_lm_head: this model's logits are not a plain linear map "
+                              "of the decoder output; using the logits path", stacklevel=2)
         bsz = batch_size or input_ids.size(0)
         all_logps: list[torch.Tensor] = []
         all_entropies: list[torch.Tensor] = []
         for start in range(0, input_ids.size(0), bsz):
             input_ids_batch = input_ids[start:start + bsz]
             attention_mask_batch = attention_mask[start:start + bsz]
+            if parts is not None:
+                # hidden states of the completion window -> fused LM head + K1
+                decoder, weight = parts
+                out = decoder(input_ids=input_ids_batch, attention_mask=attention_mask_batch,
+                              use_cache=False)
+                hidden = out[0][:, -(logits_to_keep + 1):-1, :]
+                completion_ids = input_ids_batch[:, -logits_to_keep:]
+                logps, ents, _ = fused_linear_logprob_entropy(hidden, weight, completion_ids,
+                                                              self.temperature)
+                all_logps.append(logps)
+                if compute_entropy:
+                    all_entropies.append(ents.detach())
+                continue
             model_inputs = {"input_ids": input_ids_batch,
                             "attention_mask": attention_mask_batch}
             if "logits_to_keep" in self.model_kwarg_keys:

@@ -199,3 +199,19 @@ def test_window_node_matches_oracle_bf16():
                                                  False)
     y = grpo.completion_window(base.detach().clone(), K).div_(T).cpu()
     check_forward_outputs((lp, h, lse), y, cids.cpu(), "window")
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
+def test_public_scaled_op_equals_division_then_k1(dtype):
+    x, t = _inputs(dtype, (3, 7, 4099), seed=91)
+    g = grads_like(t.shape, seed=92)
+    T = 0.85
+    xa = x.clone().requires_grad_(True)
+    outs = kernel_opt.fused_logprob_entropy_scaled(xa, t, T)
+    da = torch.autograd.grad(outs, xa, tuple(v.cuda() for v in g))[0]
+    xb = x.clone().requires_grad_(True)
+    ref = kernel_opt.fused_logprob_entropy(xb / T, t)
+    db = torch.autograd.grad(ref, xb, tuple(v.cuda() for v in g))[0]
+    for a, b in zip(outs, ref):
+        _equal(a.detach(), b.detach(), "outputs")
+    _equal(da, db, "gradient")

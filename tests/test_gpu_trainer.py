@@ -123,3 +123,75 @@ def test_multimodal_falls_back_to_parent(trainer_cls):
     tr = trainer_cls()
     with pytest.raises(AssertionError, match="parent called"):
         tr._get_per_token_logps_and_entropies(None, None, None, 3, pixel_values=object())
+
+
+class _TinyDecoder(torch.nn.Module):
+    def __init__(self, vocab, hidden):
+        super().__init__()
+        g = torch.Generator().manual_seed(5)
+        self.emb = torch.nn.Parameter((torch.randn(vocab, hidden, generator=g) * 0.5))
+
+    def forward(self, input_ids, attention_mask=None, use_cache=False):
+        h = self.emb[input_ids].cumsum(1) / torch.arange(1, input_ids.shape[1] + 1,
+                                                         device=input_ids.device)[:, None]
+        return (h.to(torch.bfloat16),)
+
+
+class _TinyHFLM(torch.nn.Module):
+    """Shaped like a transformers causal LM: decoder + bias-free lm_head."""
+
+    def __init__(self, vocab=3000, hidden=64):
+        super().__init__()
+        self.decoder = _TinyDecoder(vocab, hidden)
+        self.lm_head = torch.nn.Linear(hidden, vocab, bias=False).to(torch.bfloat16)
+        self.config = types.SimpleNamespace()
+
+    def get_decoder(self):
+        return self.decoder
+
+    def get_output_embeddings(self):
+        return self.lm_head
+
+    def forward(self, input_ids, attention_mask=None, logits_to_keep=None, use_cache=False):
+        h = self.decoder(input_ids, attention_mask)[0]
+        if logits_to_keep:
+            h = h[:, -logits_to_keep:]
+        return types.SimpleNamespace(logits=self.lm_head(h))
+
+
+@pytest.mark.parametrize("batch_size", [None, 2])
+def test_fused_lm_head_option(trainer_cls, batch_size):
+    model = _TinyHFLM().cuda()
+    input_ids = torch.randint(0, 3000, (5, 40), generator=torch.Generator().manual_seed(6)).cuda()
+    mask = torch.ones_like(input_ids)
+    K = 17
+    res = {}
+    for fused in (False, True):
+        tr = trainer_cls(k1_fused_lm_head=fused)
+        tr.temperature = 0.7
+        tr.model_kwarg_keys = {"input_ids", "attention_mask", "logits_to_keep", "use_cache"}
+        model.zero_grad()
+        lp, ent = tr._get_per_token_logps_and_entropies(model, input_ids, mask, K,
+                                                        batch_size=batch_size,
+                                                        compute_entropy=True)
+        (lp * torch.linspace(-1, 1, K, device="cuda")).sum().backward()
+        res[fused] = (lp.detach(), ent, model.lm_head.weight.grad.clone(),
+                      model.decoder.emb.grad.clone())
+    a, b = res[False], res[True]
+    torch.testing.assert_close(b[0], a[0], rtol=1e-5, atol=1e-5)
+    torch.testing.assert_close(b[1], a[1], rtol=1e-4, atol=1e-5)
+    for ga, gb in zip(a[2:], b[2:]):
+        torch.testing.assert_close(gb.float(), ga.float(), rtol=2e-2,
+                                   atol=2e-3 * float(ga.float().abs().max()))
+
+
+def test_fused_lm_head_falls_back_for_soft_capped_models(trainer_cls):
+    model = _TinyHFLM().cuda()
+    model.config.final_logit_softcapping = 30.0
+    tr = trainer_cls(k1_fused_lm_head=True)
+    tr.temperature = 1.0
+    tr.model_kwarg_keys = {"input_ids", "attention_mask", "logits_to_keep", "use_cache"}
+    ids = torch.randint(0, 3000, (2, 12), generator=torch.Generator().manual_seed(7)).cuda()
+    with pytest.warns(UserWarning, match="k1_fused_lm_head"):
+        lp, _ = tr._get_per_token_logps_and_entropies(model, ids, torch.ones_like(ids), 5)
+    assert lp.shape == (2, 5)

@@ -103,3 +103,47 @@ def test_binding_exports_every_function_the_package_calls():
     assert used, "no _C calls found"
     missing = sorted(n for n in used if not hasattr(_C, n))
     assert not missing, f"kernel_opt._C lacks {missing}; rebuild the extension"
+
+
+def test_lm_head_chunk_rows():
+    from kernel_opt import lm_head
+    q = lm_head.ROW_QUANTUM
+    for N, V, es in ((16384, 151936, 2), (1000, 152064, 2), (8192, 128256, 4), (300, 32000, 2),
+                     (50000, 256000, 2)):
+        c = lm_head.default_chunk_rows(N, V, es)
+        assert c % q == 0 and c >= q
+        assert c * V * es <= lm_head.CHUNK_BUDGET_BYTES or c == q
+        n_chunks = -(-N // c)
+        # fewest chunks that respect the budget, and no chunk much smaller than the others
+        assert n_chunks == max(1, -(-N // max(q, lm_head.CHUNK_BUDGET_BYTES // (V * es) // q * q)))
+        assert N - (n_chunks - 1) * c > 0
+    assert lm_head.default_chunk_rows(16384, 151936, 2) == 3328
+    assert lm_head.default_chunk_rows(100, 10 ** 9, 4) == q
+
+
+def test_fused_head_parts_gates_on_plain_linear_heads():
+    import types
+
+    from kernel_opt import lm_head
+
+    class M(torch.nn.Module):
+        def __init__(self, bias=False, **cfg):
+            super().__init__()
+            self.dec = torch.nn.Identity()
+            self.head = torch.nn.Linear(4, 10, bias=bias)
+            self.config = types.SimpleNamespace(**cfg)
+
+        def get_decoder(self):
+            return self.dec
+
+        def get_output_embeddings(self):
+            return self.head
+
+    m = M()
+    dec, w = lm_head.fused_head_parts(m)
+    assert dec is m.dec and w is m.head.weight
+    assert lm_head.fused_head_parts(M(bias=True)) is None
+    assert lm_head.fused_head_parts(M(final_logit_softcapping=30.0)) is None
+    assert lm_head.fused_head_parts(M(logit_scale=0.125)) is None
+    assert lm_head.fused_head_parts(M(logit_scale=1.0)) is not None
+    assert lm_head.fused_head_parts(torch.nn.Linear(2, 2)) is None
