@@ -46,6 +46,8 @@ CONFIGS = {
                dtype=torch.bfloat16, scale=3.0, window=False),
     "c3": dict(workload="baseline-config-3: GRPO window logits[:, :-1] of [16,1025,V]", B=16,
                S=1024, V=151936, dtype=torch.bfloat16, scale=2.5, window=True),
+    "c3s": dict(workload="config-3 window, 2 sequences (profiling case: 623 MB parent)", B=2,
+                S=1024, V=151936, dtype=torch.bfloat16, scale=2.5, window=True),
     "c4-bf16": dict(workload="baseline-config-4: stress, bf16", B=1, S=8192, V=128256,
                     dtype=torch.bfloat16, scale=2.0, window=False, spikes=True),
     "c4-fp16": dict(workload="baseline-config-4: stress, fp16", B=1, S=8192, V=128256,
@@ -114,11 +116,26 @@ def make_workload(cfg: dict, device, seed: int):
     for bi in range(B):
         for a in range(0, S, chunk):
             b = min(S, a + chunk)
-            probs = torch.softmax(logits[bi, a:b].float(), dim=-1)
-            targets[bi, a:b] = torch.multinomial(probs, 1, generator=gen).view(-1)
-            del probs
-    g_lp = torch.full((B, S), -1.0 / N, device=device)
-    g_h = torch.full((B, S), -0.01 / N, device=device)
+            if cfg.get("spikes"):
+                # config 4: half the rows target their argmax, half a uniform column
+                am = logits[bi, a:b].argmax(-1)
+                un = torch.randint(0, V, (b - a,), generator=gen, device=device)
+                pick = torch.rand((b - a,), generator=gen, device=device) < 0.5
+                targets[bi, a:b] = torch.where(pick, am, un)
+            else:
+                probs = torch.softmax(logits[bi, a:b].float(), dim=-1)
+                targets[bi, a:b] = torch.multinomial(probs, 1, generator=gen).view(-1)
+                del probs
+    if cfg["window"]:
+        # config 3: completion mask, ones up to a random length per sequence (mean about
+        # 0.7 S), zeros after; the loss averages over the unmasked tokens
+        lens = torch.randint(int(0.4 * S), S + 1, (B,), generator=gen, device=device)
+        mask = (torch.arange(S, device=device)[None, :] < lens[:, None]).float()
+        g_lp = -mask / mask.sum()
+        g_h = -0.01 * mask / mask.sum()
+    else:
+        g_lp = torch.full((B, S), -1.0 / N, device=device)
+        g_h = torch.full((B, S), -0.01 / N, device=device)
     return logits, targets, g_lp, g_h
 
 
@@ -195,9 +212,51 @@ def cpu_trl_step_fn(logits_cpu, targets_cpu, g_lp_cpu, g_h_cpu):
     return step
 
 
-def time_cpu_baseline(logits, targets, g_lp, g_h, esize, budget_s=12.0):
-    x = logits.detach().cpu()
-    t, a, b = targets.cpu(), g_lp.cpu(), g_h.cpu()
+def host_cores():
+    return {"os_cpu_count": os.cpu_count(), "affinity": len(os.sched_getaffinity(0)),
+            "torch_threads": torch.get_num_threads()}
+
+
+def time_oracle_fp64(x, t, a, b, budget_s=4.0):
+    """The fp64 C oracle (oracle/k1_oracle.c, OpenMP) on a bounded row sample."""
+    from oracle import oracle as k1_oracle
+    rows = min(t.numel(), 64)
+    xs = x.reshape(-1, x.shape[-1])[:rows].contiguous()
+    ts, as_, bs = t.reshape(-1)[:rows], a.reshape(-1)[:rows], b.reshape(-1)[:rows]
+    t0 = time.perf_counter()
+    n = 0
+    while True:
+        _lp, h0, l0 = k1_oracle.forward(xs, ts)
+        k1_oracle.backward(xs, ts, l0, h0, as_.numpy(), bs.numpy(), None)
+        n += 1
+        if time.perf_counter() - t0 >= budget_s:
+            break
+    dt = (time.perf_counter() - t0) / n
+    return {"rows_per_s": round(rows / dt, 2),
+            "sample": f"first {rows} rows x {x.shape[-1]}, fwd+bwd, {n} repetitions"}
+
+
+def time_cpu_baseline(logits, targets, g_lp, g_h, esize, budget_s=12.0, max_rows=1024):
+    """TRL eager path restated, on the host cores; configs above max_rows rows are
+    subsampled to their first 256 rows (full V) and labelled so."""
+    N_all = targets.numel()
+    V = logits.shape[-1]
+    sub = N_all > max_rows
+    rows = min(256, N_all) if sub else N_all
+
+    def first_rows(v):
+        # the first `rows` rows in order, sequence by sequence (no copy of the whole
+        # strided window)
+        parts, need = [], rows
+        for bi in range(v.shape[0]):
+            if need == 0:
+                break
+            take = v[bi, :need]
+            parts.append(take.detach().cpu())
+            need -= take.shape[0]
+        return torch.cat(parts).unsqueeze(0)
+
+    x, t, a, b = (first_rows(v) for v in (logits, targets, g_lp, g_h))
     step = cpu_trl_step_fn(x, t, a, b)
     step()
     t0 = time.perf_counter()
@@ -208,12 +267,16 @@ def time_cpu_baseline(logits, targets, g_lp, g_h, esize, budget_s=12.0):
         if time.perf_counter() - t0 >= budget_s:
             break
     dt = (time.perf_counter() - t0) / n
-    N, V = t.numel(), x.shape[-1]
+    N = t.numel()
     fwd, bwd = algorithmic_bytes(N, V, esize)
+    what = (f"subsampled: first {N} of {N_all} rows x {V}" if sub
+            else f"the full batch ({N} rows x {V})")
     return {"value": round((fwd + bwd) / dt / 1e9, 4), "unit": UNIT,
             "rows_per_s": round(N / dt, 2), "cores": torch.get_num_threads(), "kind": "port",
-            "sample": f"the full batch ({N} rows x {V}), {n} fwd+bwd steps in "
-                      f"{n * dt:.1f} s, TRL-1.4 eager path restated (oracle/trl_eager.py)"}
+            "sample": f"{what}, {n} fwd+bwd steps in {n * dt:.1f} s, TRL-1.4 eager path "
+                      f"restated (oracle/trl_eager.py)",
+            "host_cores": host_cores(),
+            "oracle_fp64": time_oracle_fp64(x, t, a, b)}
 
 
 # ---------------------------------------------------------------------------------------

@@ -67,8 +67,9 @@ struct BwdParams {
 // ---------------------------------------------------------------------------------
 // Scaled logits (sampling temperature).  The scaled entry points read every logit as
 // y = dtype(x * s): the fp32 product rounded to the logits' own type, which is what an
-// in-place `logits.div_(T)` leaves in the tensor (torch divides a tensor by a Python
-// scalar as a multiplication by the fp32 reciprocal s = 1/T).  Their gradient w.r.t. x is
+// in-place `logits.div_(T)` leaves in the tensor (torch divides a CUDA tensor by a
+// Python scalar as a multiplication by s = (float)(1.0 / T), the reciprocal taken in
+// double and rounded to fp32).  Their gradient w.r.t. x is
 // dtype(dtype(dL/dy) * s): the rounding of K1's own backward, then the division's
 // backward.  With s = 1 both maps are the identity, so the per-row target-logit loads
 // apply p.scale unconditionally; the per-element paths are compiled with and without it.

@@ -23,7 +23,7 @@ import torch
 
 from kernel_opt import _C
 
-from .ops import _alloc_outputs, _check_inputs, fused_logprob_entropy
+from .ops import _alloc_outputs, _check_inputs
 
 MULTIMODAL_KWARGS = (
     "pixel_values", "image_grid_thw", "num_images",
@@ -40,20 +40,16 @@ def completion_window(logits: torch.Tensor, logits_to_keep: int) -> torch.Tensor
 
 
 def temperature_scale(temperature: float) -> float:
-    """The factor torch multiplies by when it divides a tensor by the Python scalar
-    `temperature`: the fp32 reciprocal 1.0f / (float)temperature, correctly rounded."""
-    t = np.float32(temperature)
+    """The factor torch multiplies by when it divides a CUDA tensor by the Python scalar
+    `temperature`: 1 / temperature taken in double precision, then rounded to fp32
+    (not 1.0f / (float)temperature, which differs in the last bit for e.g. 0.85)."""
+    t = float(temperature)
     if not (np.isfinite(t) and t > 0):
         raise ValueError(f"temperature must be positive and finite, got {temperature!r}")
-    return float(np.float32(1.0) / t)
-
-
-def k1_logps_and_entropies(logits: torch.Tensor, completion_ids: torch.Tensor,
-                           compute_entropy: bool):
-    """Per-token log-probs (with grad) and detached entropies of an already sliced and
-    scaled [B, L', V] window in one K1 launch.  Returns (logps [B, L'], entropies or None)."""
-    logps, ents, _lse = fused_logprob_entropy(logits, completion_ids.contiguous())
-    return logps, (ents.detach() if compute_entropy else None)
+    s = np.float32(1.0 / t)
+    if not (np.isfinite(s) and s > 0):
+        raise ValueError(f"temperature {temperature!r} has no finite positive fp32 reciprocal")
+    return float(s)
 
 
 def _prep(g):

@@ -165,8 +165,10 @@ int k1_fused_logprob_entropy_v1_backward(
  * for the reference trainer's `logits.div_(self.temperature)` followed by K1 on the
  * completion window (reference python/kernel_opt/trainer.py:101-127).  Every logit x is read
  * as y = dtype(x * scale): the fp32 product rounded to nearest-even in the logits' type, which
- * is the tensor torch's in-place division leaves behind (torch divides by a Python scalar T
- * as a multiplication by the fp32 reciprocal, so pass scale = 1.0f / (float)T).  The forward
+ * is the tensor torch's in-place division leaves behind (torch divides a CUDA tensor by a
+ * Python scalar T as a multiplication by the reciprocal taken in double and rounded to
+ * fp32, so pass scale = (float)(1.0 / T); 1.0f / (float)T differs in the last bit for
+ * some T, e.g. 0.85).  The forward
  * results are those of k1_fused_logprob_entropy_v1 on y, bit for bit; the backward writes the
  * gradient with respect to x, d_logits = dtype(dtype(dL/dy) * scale): K1's backward on y
  * followed by the division's own backward, again bit for bit.  The division pass, its

@@ -70,9 +70,11 @@ def test_completion_window_is_a_strided_view():
     torch.testing.assert_close(w, base[:, :-1][:, -6:])
 
 
-def test_temperature_scale_is_the_fp32_reciprocal():
-    for T in (0.7, 0.9, 1.3, 2.0, 1e-3, 1.0):
-        assert grpo.temperature_scale(T) == float(np.float32(1.0) / np.float32(T))
+def test_temperature_scale_is_the_rounded_double_reciprocal():
+    # torch multiplies by (float)(1.0 / T); 1.0f / (float)T differs for T = 0.85
+    for T in (0.7, 0.85, 0.9, 1.3, 2.0, 1e-3, 1.0):
+        assert grpo.temperature_scale(T) == float(np.float32(1.0 / T))
+    assert grpo.temperature_scale(0.85) != float(np.float32(1.0) / np.float32(0.85))
     assert grpo.temperature_scale(1.0) == 1.0
     for bad in (0.0, -1.0, float("inf"), float("nan")):
         with pytest.raises(ValueError):
