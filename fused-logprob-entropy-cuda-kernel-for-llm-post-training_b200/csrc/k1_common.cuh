@@ -143,6 +143,17 @@ __device__ __forceinline__ float2 bf16x2_minus(uint32_t w, float nm) {
     return make_float2(d0, d1);
 }
 
+// The same for two fp16 logits (f16 -> f32 is exact, the add rounds once: identical to
+// converting first and subtracting in fp32).
+__device__ __forceinline__ float2 f16x2_minus(uint32_t w, float nm) {
+    float d0, d1;
+    asm("{\n\t.reg .b16 lo, hi;\n\tmov.b32 {lo, hi}, %2;\n\t"
+        "add.rn.f32.f16 %0, lo, %3;\n\tadd.rn.f32.f16 %1, hi, %3;\n\t}"
+        : "=f"(d0), "=f"(d1)
+        : "r"(w), "f"(nm));
+    return make_float2(d0, d1);
+}
+
 template <>
 struct DT<__half> {
     static constexpr int kEPV = 8;

@@ -157,6 +157,8 @@ __device__ __forceinline__ void fwd_chunk(const uint4 (&v)[U], FwdState& st, boo
         for (int i = 0; i < 4 * U; ++i) {
             if constexpr (K1_MIXED_ADD && std::is_same<T, __nv_bfloat16>::value) {
                 st.accum_d(bf16x2_minus(w[i], nm.x));
+            } else if constexpr (K1_MIXED_ADD && std::is_same<T, __half>::value) {
+                st.accum_d(f16x2_minus(w[i], nm.x));
             } else {
                 st.accum(D::to_f2(w[i]), nm);
             }
