@@ -449,32 +449,44 @@ def ours_arm(args, cfg, rank, local_rank, world):
     targets_h = targets.cpu().pin_memory()
     glp_h, gh_h = g_lp.cpu().pin_memory(), g_h.cpu().pin_memory()
     d_h = torch.empty(logits.shape, dtype=dt, **pin)
+    d_dev = torch.empty(logits.shape, dtype=dt, device=device)
     outs_h = [torch.empty(targets.shape, dtype=torch.float32, **pin) for _ in range(3)]
     h2d = logits_h.numel() * esize + targets_h.numel() * 8 + 2 * glp_h.numel() * 4
-    d2h = d_h.numel() * esize + 3 * outs_h[0].numel() * 4
+    d2h_outputs = 3 * outs_h[0].numel() * 4
+    d2h_with_grad = d_h.numel() * esize + d2h_outputs
 
     from kernel_opt import host as k1_host
 
-    def e2e_step():
-        # public host-buffer API: chunks of rows copied in, reduced + differentiated and
-        # copied out on three overlapping streams; returns once the host buffers are filled
+    def e2e_step(d_logits):
+        # public host-buffer API: chunks of rows copied in and reduced + differentiated on
+        # overlapping streams; the per-row outputs (and, for a host d_logits, the gradient)
+        # are copied out; returns once the host buffers are filled
         k1_host.fused_logprob_entropy_fwd_bwd_host(logits_h, targets_h, glp_h, gh_h, None,
-                                                   d_logits=d_h, outputs=outs_h, device=device)
+                                                   d_logits=d_logits, outputs=outs_h,
+                                                   device=device)
 
-    for _ in range(2):
-        e2e_step()
-    barrier()
     K2 = max(1, min(K, 20))
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    for _ in range(K2):
-        e2e_step()
-    e1.record(stream)
-    barrier()
-    e2e_ms = torch.tensor([e0.elapsed_time(e1)], device=device, dtype=torch.float64)
-    if world > 1:
-        dist.all_reduce(e2e_ms, op=dist.ReduceOp.MAX)
-    e2e_ms = float(e2e_ms.item())
+
+    def time_e2e(d_logits):
+        for _ in range(2):
+            e2e_step(d_logits)
+        barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(K2):
+            e2e_step(d_logits)
+        e1.record(stream)
+        barrier()
+        ms = torch.tensor([e0.elapsed_time(e1)], device=device, dtype=torch.float64)
+        if world > 1:
+            dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+        return float(ms.item())
+
+    # the step's result (per-row log-prob / entropy / lse) comes back to the host; the
+    # logits gradient stays in HBM, where a training step's next backward op reads it
+    e2e_ms = time_e2e(d_dev)
+    # offload variant: the gradient also goes back to host memory
+    e2e_host_grad_ms = time_e2e(d_h)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -512,8 +524,14 @@ def ours_arm(args, cfg, rank, local_rank, world):
                      "traffic": committed_traffic(cfg_name)},
         "gpu_launches": 2 * K,
         "e2e": {"value": round(step_bytes * K2 * world / (e2e_ms / 1e3) / 1e9, 3), "unit": UNIT,
-                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                "ms_per_step": round(e2e_ms / K2, 3), "steps": K2},
+                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h_outputs,
+                "ms_per_step": round(e2e_ms / K2, 3), "steps": K2,
+                "note": "logits, targets and upstream grads from pinned host memory; "
+                        "logprob/entropy/lse read back; the logits gradient stays on the GPU"},
+        "e2e_gradient_to_host": {
+            "value": round(step_bytes * K2 * world / (e2e_host_grad_ms / 1e3) / 1e9, 3),
+            "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h_with_grad,
+            "ms_per_step": round(e2e_host_grad_ms / K2, 3), "steps": K2},
         "clocks": clocks.summary(),
     }
     if cpu is not None:

@@ -8,6 +8,11 @@ the host link instead of both.  Use it when the [N, V] logits (and their gradien
 kept in host memory, e.g. offloaded activations; with device-resident logits call
 `kernel_opt.fused_logprob_entropy` instead.
 
+Chunks ramp up at the start and down at the end (1/8, 1/4, 1/2 of the full chunk, then
+full chunks, then the mirror image): the first chunk's copy in and the last chunk's copy
+out are the only transfers that cannot overlap the other direction, so they are kept
+small.
+
 The upstream gradients are per row and known before the call (as for a policy-gradient
 loss whose per-token weights come from advantages and masks), so each chunk's backward
 can run right after its forward.  Rows are independent, so chunking changes no result.
@@ -27,6 +32,29 @@ def _streams(dev: torch.device):
     if dev not in _STREAMS:
         _STREAMS[dev] = tuple(torch.cuda.Stream(dev) for _ in range(3))
     return _STREAMS[dev]
+
+
+def chunk_schedule(n_rows: int, chunk_rows: int, ramp: int = 3) -> list[tuple[int, int]]:
+    """Row ranges [a, b) covering [0, n_rows) in order: `ramp` chunks growing by powers of
+    two up to chunk_rows, full chunks, then `ramp` chunks shrinking back."""
+    R = max(1, chunk_rows)
+    ramp_sizes = [max(1, R >> k) for k in range(ramp, 0, -1)]  # R/8, R/4, R/2
+    head = list(ramp_sizes)
+    tail = list(reversed(ramp_sizes))
+    if sum(head) + sum(tail) >= n_rows:  # too few rows to ramp: uniform chunks
+        head, tail = [], []
+    sizes = list(head)
+    middle = n_rows - sum(head) - sum(tail)
+    sizes += [R] * (middle // R)
+    if middle % R:
+        sizes.append(middle % R)
+    sizes += tail
+    out, a = [], 0
+    for s in sizes:
+        out.append((a, a + s))
+        a += s
+    assert a == n_rows
+    return out
 
 
 def _rows2d(t: torch.Tensor, V: int) -> torch.Tensor:
@@ -50,14 +78,17 @@ def fused_logprob_entropy_fwd_bwd_host(logits: torch.Tensor, targets: torch.Tens
                  needed for the copies to overlap.
         targets: [...] int64 (CPU or CUDA).
         g_logp, g_ent, g_lse: upstream gradients [...] (fp32, CPU or CUDA) or None (zero).
-        d_logits: CPU tensor like `logits` for the gradient (allocated pinned if None);
-                 may be `logits` itself, which is then overwritten chunk by chunk.
+        d_logits: tensor like `logits` for the gradient: a CPU tensor (allocated pinned
+                 if None; may be `logits` itself, which is then overwritten chunk by
+                 chunk), or a CUDA tensor on `device`, into which each chunk's backward
+                 writes directly (the gradient then stays on the device, as it does in a
+                 training step, and only the per-row outputs travel back).
         outputs: optional (logprob, entropy, lse) CPU fp32 tensors shaped like targets.
         chunk_rows: rows per chunk (default: about 32 MB of logits per chunk).
         device: CUDA device (default: current).
 
-    Returns (logprob, entropy, lse, d_logits) on the host.  The call returns when all
-    host buffers hold their results.
+    Returns (logprob, entropy, lse, d_logits); the outputs are on the host.  The call
+    returns when all host buffers hold their results.
     """
     dev = torch.device("cuda", torch.cuda.current_device() if device is None else
                        (device.index if isinstance(device, torch.device) else device))
@@ -71,6 +102,11 @@ def fused_logprob_entropy_fwd_bwd_host(logits: torch.Tensor, targets: torch.Tens
     if d_logits is None:
         d_logits = torch.empty_like(logits, pin_memory=True)
     d = _rows2d(d_logits, V)
+    grad_on_device = d_logits.is_cuda
+    if grad_on_device and d_logits.device != dev:
+        raise ValueError("a device d_logits must be on `device`")
+    if d_logits.shape != logits.shape or d_logits.dtype != logits.dtype:
+        raise ValueError("d_logits must match logits in shape and dtype")
     if outputs is None:
         outputs = tuple(torch.empty(targets.shape, dtype=torch.float32, pin_memory=True)
                         for _ in range(3))
@@ -82,7 +118,8 @@ def fused_logprob_entropy_fwd_bwd_host(logits: torch.Tensor, targets: torch.Tens
     if chunk_rows is None:
         chunk_rows = max(1, (32 << 20) // (V * esize))
     R = min(chunk_rows, N)
-    nchunks = (N + R - 1) // R
+    ranges = chunk_schedule(N, R)
+    nchunks = len(ranges)
 
     # small per-row inputs go to the device once
     t_dev = targets.reshape(-1).to(dev, non_blocking=True)
@@ -102,8 +139,7 @@ def fused_logprob_entropy_fwd_bwd_host(logits: torch.Tensor, targets: torch.Tens
     for s in (s_in, s_run, s_out):
         s.wait_event(start)
 
-    for i in range(nchunks):
-        a, b = i * R, min(N, (i + 1) * R)
+    for i, (a, b) in enumerate(ranges):
         k = i % len(bufs)
         buf = bufs[k][: b - a]
         with torch.cuda.stream(s_in):
@@ -117,11 +153,15 @@ def fused_logprob_entropy_fwd_bwd_host(logits: torch.Tensor, targets: torch.Tens
             tt = t_dev[a:b]
             _C.fused_logprob_entropy_v1(buf, tt, lp, h, l)
             gg = [None if g is None else g[a:b] for g in grads]
-            _C.fused_logprob_entropy_v1_backward(buf, tt, l, h, *gg, buf)  # in place
+            if grad_on_device:
+                _C.fused_logprob_entropy_v1_backward(buf, tt, l, h, *gg, d[a:b])
+            else:
+                _C.fused_logprob_entropy_v1_backward(buf, tt, l, h, *gg, buf)  # in place
             ev_run[k].record(s_run)
         with torch.cuda.stream(s_out):
             s_out.wait_event(ev_run[k])
-            d[a:b].copy_(buf, non_blocking=True)
+            if not grad_on_device:
+                d[a:b].copy_(buf, non_blocking=True)
             ev_out[k].record(s_out)
 
     with torch.cuda.stream(s_out):

@@ -56,3 +56,28 @@ def test_host_streaming_in_place_and_shapes():
     assert d.data_ptr() == buf.data_ptr() and lp.shape == (B, S)
     torch.testing.assert_close(d.view(-1, V), ref[3], rtol=0, atol=0)
     torch.testing.assert_close(lp.view(-1), ref[0], rtol=0, atol=0)
+
+
+@pytest.mark.parametrize("chunk_rows", [None, 9])
+def test_host_streaming_gradient_stays_on_device(chunk_rows):
+    """d_logits on the device: each chunk's backward writes straight into it and only the
+    per-row outputs come back to the host."""
+    N, V = 120, 32000
+    x = seeded_logits((N, V), torch.bfloat16, 3.0, seed=60).pin_memory()
+    t = seeded_targets((N,), V, seed=61)
+    g = grads_like((N,), seed=62)
+    ref = device_reference(x, t, g)
+    d_dev = torch.empty((N, V), dtype=x.dtype, device="cuda")
+    lp, h, l, d = fused_logprob_entropy_fwd_bwd_host(x, t, *g, d_logits=d_dev,
+                                                     chunk_rows=chunk_rows)
+    assert d is d_dev and not lp.is_cuda
+    if chunk_rows is None:
+        for a, b in zip((lp, h, l, d.cpu()), ref):
+            torch.testing.assert_close(a, b, rtol=0, atol=0)
+    else:
+        for a, b in zip((lp, h, l), ref[:3]):
+            torch.testing.assert_close(a, b, rtol=2.4e-7, atol=0)
+        scale = float(ref[3].float().abs().max())
+        torch.testing.assert_close(d.cpu().float(), ref[3].float(), rtol=8e-3, atol=1e-6 * scale)
+    with pytest.raises(ValueError):
+        fused_logprob_entropy_fwd_bwd_host(x, t, *g, d_logits=d_dev[:, :100])

@@ -149,3 +149,15 @@ def test_fused_head_parts_gates_on_plain_linear_heads():
     assert lm_head.fused_head_parts(M(logit_scale=0.125)) is None
     assert lm_head.fused_head_parts(M(logit_scale=1.0)) is not None
     assert lm_head.fused_head_parts(torch.nn.Linear(2, 2)) is None
+
+
+def test_host_chunk_schedule_covers_rows_once_and_ramps():
+    from kernel_opt.host import chunk_schedule
+    for n, r in ((1024, 110), (5, 110), (300, 110), (110, 110), (1000, 7), (16384, 3328), (1, 1)):
+        s = chunk_schedule(n, r)
+        assert s[0][0] == 0 and s[-1][1] == n
+        assert all(b > a for a, b in s) and all(s[i][1] == s[i + 1][0] for i in range(len(s) - 1))
+        assert max(b - a for a, b in s) <= r
+    s = chunk_schedule(1024, 110)
+    sizes = [b - a for a, b in s]
+    assert sizes[:3] == [13, 27, 55] and sizes[-3:] == [55, 27, 13]
