@@ -8,6 +8,12 @@
 // block a few whole rows, a handful of rows spreads each row over many blocks
 // (the split-vocab case).  A row that crosses block boundaries is finished by the
 // last block to arrive at its ticket; nobody waits.
+//
+// The forward can also keep the last part of the range as a dynamic tail (Partition):
+// fixed chunks that blocks take from an atomic counter once their own piece is done, so
+// that the blocks sharing an SM (which the warp schedulers do not serve equally) finish
+// together.  Chunk boundaries are fixed and a chunk is computed the same way by any
+// block, so results do not depend on which block took it.
 #pragma once
 
 #include <type_traits>
@@ -27,6 +33,22 @@ __device__ __forceinline__ int64_t block_of(int64_t u, int64_t total, int64_t G)
     return ((u + 1) * G + total - 1) / total - 1;
 }
 
+// Owners of the forward's units: G static pieces over [0, split) (piece b is block b's)
+// followed by D dynamic chunks of `csize` units over [split, total) (the last one may be
+// shorter), taken in order from a counter.  D = 0 (split = total) is the plain static
+// split.  Every owner is non-empty (G <= split, D = ceil((total - split) / csize),
+// enforced by the launcher).  start(o) is defined for 0 <= o <= G + D; start(G) = split
+// comes from the static formula, and no division involves D or csize when D = 0.
+struct Partition {
+    int64_t total, split, G, D, csize;
+    __device__ __forceinline__ int64_t start(int64_t o) const {
+        return o <= G ? piece_start(o, split, G) : min(total, split + (o - G) * csize);
+    }
+    __device__ __forceinline__ int64_t owner_of(int64_t u) const {
+        return u < split ? block_of(u, split, G) : G + (u - split) / csize;
+    }
+};
+
 struct FwdParams {
     const void* logits;
     int64_t n_rows;
@@ -40,9 +62,16 @@ struct FwdParams {
     float* entropy;
     float* lse;
     k1_partial* partials;  // shard mode output
-    RowPartial* ws_part;   // 2 * gridDim.x slots
-    unsigned* ws_ticket;   // gridDim.x counters, zero between calls
+    RowPartial* ws_part;   // 2 slots per owner (the owner's first and last row)
+    unsigned* ws_ticket;   // one counter per owner, zero between calls
+    unsigned* ws_dyn;      // [next dynamic chunk, blocks done], zero between calls
+    int64_t split;         // start of the dynamic tail (= total without one)
+    int64_t n_dyn;         // dynamic chunks (0 = static split only)
+    int64_t dyn_units;     // units per dynamic chunk
     float scale;           // logits are read as dtype(x * scale); 1 = as stored
+    __device__ __forceinline__ Partition part() const {
+        return Partition{total, split, (int64_t)gridDim.x, n_dyn, dyn_units};
+    }
 };
 
 struct BwdParams {
@@ -350,7 +379,8 @@ struct FwdSmem {
     double wt[2][NW];
     RowPartial done_part[kRowCap];
     int64_t done_row[kRowCap];
-    unsigned split_prev[2];  // ticket values of the block's first / last split row
+    unsigned split_prev[2];  // ticket values of the owner's first / last split row
+    unsigned next_chunk[2];  // next dynamic chunk, double-buffered by grab parity
 };
 
 // Merge the threads' states of one segment into `out` (relative to the segment maximum).
@@ -427,9 +457,9 @@ __device__ __forceinline__ void fwd_flush_rows(const FwdParams& p, FwdSmem<THREA
 template <typename T, bool SHARD>
 __device__ __forceinline__ void fwd_merge_split_row(const FwdParams& p, int64_t r) {
     const int lane = threadIdx.x & 31;
-    const int64_t G = gridDim.x;
-    const int64_t bf = block_of(r * p.vpr, p.total, G);
-    const int64_t bl = block_of((r + 1) * p.vpr - 1, p.total, G);
+    const Partition P = p.part();
+    const int64_t bf = P.owner_of(r * p.vpr);
+    const int64_t bl = P.owner_of((r + 1) * p.vpr - 1);
     const T* rowp = reinterpret_cast<const T*>(p.logits) + p.lay.offset(r);
     float xt = 0.f;
     bool has = false;
@@ -446,7 +476,7 @@ __device__ __forceinline__ void fwd_merge_split_row(const FwdParams& p, int64_t 
     acc.m = -INFINITY;
     acc.pad = 0.f;
     for (int64_t c = bf + lane; c <= bl; c += 32) {
-        const int64_t fr = piece_start(c, p.total, G) / p.vpr;
+        const int64_t fr = P.start(c) / p.vpr;
         const RowPartial* q = p.ws_part + 2 * c + (r == fr ? 0 : 1);
         RowPartial qq;
         qq.z = __ldcg(&q->z);
@@ -485,23 +515,21 @@ __device__ __forceinline__ void fwd_merge_split_row(const FwdParams& p, int64_t 
     }
 }
 
-template <typename T, int THREADS, int U, bool VEC, bool SHARD, bool SCALED = false>
-__global__ void __launch_bounds__(THREADS, K1_FWD_MINB) k1_fwd_kernel(FwdParams p) {
+// One owner's units (a block's static piece or a dynamic chunk): stream its row segments,
+// park whole rows for the batched flush, publish partials of rows shared with other
+// owners and merge those for which this owner drew the last ticket.
+template <typename T, int THREADS, int U, bool VEC, bool SHARD, bool SCALED>
+__device__ __forceinline__ void fwd_owner(const FwdParams& p, const Partition& P, int64_t owner,
+                                          FwdSmem<THREADS>& sm, int& count, int& buf) {
     constexpr int BAR = 0;
-    __shared__ FwdSmem<THREADS> sm;
-    pdl_wait();
-    pdl_trigger();
     const int tid = threadIdx.x;
-    const int64_t G = gridDim.x, b = blockIdx.x;
-    const int64_t start0 = piece_start(b, p.total, G);
-    const int64_t end = piece_start(b + 1, p.total, G);
-    int64_t start = start0;
+    int64_t start = P.start(owner);
+    const int64_t end = P.start(owner + 1);
     int64_t r = start / p.vpr;
     int64_t j0 = start - r * p.vpr;
     const int64_t first_row = r;
     int64_t split_row[2] = {-1, -1};
-    unsigned split_prev[2] = {0u, 0u};  // thread 0 only; read after the loop
-    int count = 0, buf = 0;
+    unsigned split_prev[2] = {0u, 0u};  // thread 0 only
 
     while (start < end) {
         const int64_t j1 = min(p.vpr, j0 + (end - start));
@@ -534,36 +562,75 @@ __global__ void __launch_bounds__(THREADS, K1_FWD_MINB) k1_fwd_kernel(FwdParams 
                 count = 0;
             }
         } else {
-            // Row shared with neighbouring blocks: publish this block's piece and draw a
-            // ticket; the block that draws the last one merges the row after its own loop.
+            // Row shared with other owners: publish this owner's part and draw a ticket;
+            // the owner that draws the last one merges the row.
             const int slot = (r == first_row) ? 0 : 1;
             split_row[slot] = r;
             if (tid == 0) {
-                p.ws_part[2 * b + slot] = part;
+                p.ws_part[2 * owner + slot] = part;
                 __threadfence();
-                split_prev[slot] = atomicAdd(p.ws_ticket + block_of(r * p.vpr, p.total, G), 1u);
+                split_prev[slot] = atomicAdd(p.ws_ticket + P.owner_of(r * p.vpr), 1u);
             }
         }
         start += j1 - j0;
         ++r;
         j0 = 0;
     }
+    if (split_row[0] < 0 && split_row[1] < 0) return;  // block-uniform
     if (tid == 0) {
         sm.split_prev[0] = split_prev[0];
         sm.split_prev[1] = split_prev[1];
     }
-    fwd_flush_rows<T, THREADS, BAR, SHARD>(p, sm, count);  // its barrier publishes split_prev
-    // split rows this block finishes: the first one by warp 0, the last one by warp 1
+    group_sync<THREADS, BAR>();
+    // the first split row by warp 0, the last one by warp 1
     const int slot = tid >> 5;
     if (slot < 2) {
         const int64_t sr = slot == 0 ? split_row[0] : split_row[1];
         if (sr >= 0) {
-            const int64_t bf = block_of(sr * p.vpr, p.total, G);
-            const int64_t bl = block_of((sr + 1) * p.vpr - 1, p.total, G);
+            const int64_t bf = P.owner_of(sr * p.vpr);
+            const int64_t bl = P.owner_of((sr + 1) * p.vpr - 1);
             const unsigned prev = slot == 0 ? sm.split_prev[0] : sm.split_prev[1];
             if (prev == (unsigned)(bl - bf)) fwd_merge_split_row<T, SHARD>(p, sr);
         }
     }
+    group_sync<THREADS, BAR>();  // split_prev is rewritten by the next owner
+}
+
+template <typename T, int THREADS, int U, bool VEC, bool SHARD, bool SCALED = false>
+__global__ void __launch_bounds__(THREADS, K1_FWD_MINB) k1_fwd_kernel(FwdParams p) {
+    constexpr int BAR = 0;
+    __shared__ FwdSmem<THREADS> sm;
+    pdl_wait();
+    pdl_trigger();
+    const Partition P = p.part();
+    const int tid = threadIdx.x;
+    int count = 0, buf = 0;
+    if (P.D == 0) {
+        fwd_owner<T, THREADS, U, VEC, SHARD, SCALED>(p, P, blockIdx.x, sm, count, buf);
+    } else {
+        // the static piece, then dynamic chunks; the next chunk's index is requested when
+        // an owner starts, so the atomic's latency overlaps that owner's streaming
+        unsigned next = 0u;
+        if (tid == 0) next = atomicAdd(p.ws_dyn, 1u);
+        int64_t owner = blockIdx.x;
+        int nb = 0;
+        while (true) {
+            fwd_owner<T, THREADS, U, VEC, SHARD, SCALED>(p, P, owner, sm, count, buf);
+            if (tid == 0) sm.next_chunk[nb] = next;
+            group_sync<THREADS, BAR>();
+            const unsigned o = sm.next_chunk[nb];
+            nb ^= 1;
+            if (o >= (unsigned)P.D) break;
+            if (tid == 0) next = atomicAdd(p.ws_dyn, 1u);
+            owner = P.G + o;
+        }
+        // the last block out leaves the counters zeroed for the next call
+        if (tid == 0 && atomicAdd(p.ws_dyn + 1, 1u) == gridDim.x - 1) {
+            p.ws_dyn[0] = 0u;
+            p.ws_dyn[1] = 0u;
+        }
+    }
+    fwd_flush_rows<T, THREADS, BAR, SHARD>(p, sm, count);
 }
 
 // ---------------------------------------------------------------------------------

@@ -115,13 +115,14 @@ int k1_fused_logprob_entropy_v1(const void* logits, int dtype, int64_t n_rows, i
 
 /*
  * Forward that allocates nothing and takes no workspace: the same kernel and results as
- * k1_fused_logprob_entropy_v1, with its split-row scratch in a 256 KiB array that the
+ * k1_fused_logprob_entropy_v1, with its split-row scratch in a 512 KiB array that the
  * library defines in device memory (held on every GPU that loads the library until the
  * process exits).  For callers that cannot call cudaMalloc or hand out device memory of
  * their own -- e.g. a plugin inside a host framework whose memory pool is the only
  * allocator, or latency-critical code that must avoid cudaMalloc's implicit device
  * synchronisation.  Fails with K1_ERR_WORKSPACE if a device needs more scratch than the
- * array holds (it needs 2 x 24 + 4 bytes per resident block, about 61 KiB on 148 SMs).
+ * array holds (it needs 2 x 24 + 4 bytes for each of 32 work owners per SM, about 241 KiB on
+ * 148 SMs).
  * The first call on a device looks up the array's device address with that device
  * current; make that first call before any stream capture.  Each call clears the part
  * of the array that must start at zero.  All calls on a device share the array: calls

