@@ -515,12 +515,34 @@ __device__ __forceinline__ void fwd_merge_split_row(const FwdParams& p, int64_t 
     }
 }
 
+// Merge the split rows (first / last row of an owner, -1 = none) for which the owner drew
+// the last ticket: the first by warp 0, the last by warp 1.  split_prev must be in shared
+// memory and visible to those warps (a barrier after thread 0 wrote it).
+template <typename T, int THREADS, bool SHARD>
+__device__ __forceinline__ void fwd_merge_owner_rows(const FwdParams& p, const Partition& P,
+                                                     const int64_t (&split_row)[2],
+                                                     const FwdSmem<THREADS>& sm) {
+    const int slot = threadIdx.x >> 5;
+    if (slot < 2) {
+        const int64_t sr = slot == 0 ? split_row[0] : split_row[1];
+        if (sr >= 0) {
+            const int64_t bf = P.owner_of(sr * p.vpr);
+            const int64_t bl = P.owner_of((sr + 1) * p.vpr - 1);
+            const unsigned prev = slot == 0 ? sm.split_prev[0] : sm.split_prev[1];
+            if (prev == (unsigned)(bl - bf)) fwd_merge_split_row<T, SHARD>(p, sr);
+        }
+    }
+}
+
 // One owner's units (a block's static piece or a dynamic chunk): stream its row segments,
-// park whole rows for the batched flush, publish partials of rows shared with other
-// owners and merge those for which this owner drew the last ticket.
-template <typename T, int THREADS, int U, bool VEC, bool SHARD, bool SCALED>
+// park whole rows for the batched flush and publish partials of rows shared with other
+// owners.  MERGE_NOW merges those for which this owner drew the last ticket before
+// returning (two barriers, only when the owner has such rows); otherwise the split rows
+// and their tickets (thread 0) are left in split_row / split_prev for the caller.
+template <typename T, int THREADS, int U, bool VEC, bool SHARD, bool SCALED, bool MERGE_NOW>
 __device__ __forceinline__ void fwd_owner(const FwdParams& p, const Partition& P, int64_t owner,
-                                          FwdSmem<THREADS>& sm, int& count, int& buf) {
+                                          FwdSmem<THREADS>& sm, int& count, int& buf,
+                                          int64_t (&split_row)[2], unsigned (&split_prev)[2]) {
     constexpr int BAR = 0;
     const int tid = threadIdx.x;
     int64_t start = P.start(owner);
@@ -528,8 +550,8 @@ __device__ __forceinline__ void fwd_owner(const FwdParams& p, const Partition& P
     int64_t r = start / p.vpr;
     int64_t j0 = start - r * p.vpr;
     const int64_t first_row = r;
-    int64_t split_row[2] = {-1, -1};
-    unsigned split_prev[2] = {0u, 0u};  // thread 0 only
+    split_row[0] = split_row[1] = -1;
+    split_prev[0] = split_prev[1] = 0u;
 
     while (start < end) {
         const int64_t j1 = min(p.vpr, j0 + (end - start));
@@ -576,24 +598,16 @@ __device__ __forceinline__ void fwd_owner(const FwdParams& p, const Partition& P
         ++r;
         j0 = 0;
     }
-    if (split_row[0] < 0 && split_row[1] < 0) return;  // block-uniform
-    if (tid == 0) {
-        sm.split_prev[0] = split_prev[0];
-        sm.split_prev[1] = split_prev[1];
-    }
-    group_sync<THREADS, BAR>();
-    // the first split row by warp 0, the last one by warp 1
-    const int slot = tid >> 5;
-    if (slot < 2) {
-        const int64_t sr = slot == 0 ? split_row[0] : split_row[1];
-        if (sr >= 0) {
-            const int64_t bf = P.owner_of(sr * p.vpr);
-            const int64_t bl = P.owner_of((sr + 1) * p.vpr - 1);
-            const unsigned prev = slot == 0 ? sm.split_prev[0] : sm.split_prev[1];
-            if (prev == (unsigned)(bl - bf)) fwd_merge_split_row<T, SHARD>(p, sr);
+    if constexpr (MERGE_NOW) {
+        if (split_row[0] < 0 && split_row[1] < 0) return;  // block-uniform
+        if (tid == 0) {
+            sm.split_prev[0] = split_prev[0];
+            sm.split_prev[1] = split_prev[1];
         }
+        group_sync<THREADS, BAR>();
+        fwd_merge_owner_rows<T, THREADS, SHARD>(p, P, split_row, sm);
+        group_sync<THREADS, BAR>();  // split_prev is rewritten by the next owner
     }
-    group_sync<THREADS, BAR>();  // split_prev is rewritten by the next owner
 }
 
 template <typename T, int THREADS, int U, bool VEC, bool SHARD, bool SCALED = false>
@@ -605,17 +619,29 @@ __global__ void __launch_bounds__(THREADS, K1_FWD_MINB) k1_fwd_kernel(FwdParams 
     const Partition P = p.part();
     const int tid = threadIdx.x;
     int count = 0, buf = 0;
+    // the block's static piece; its split rows are merged at the very end, after the
+    // flush barrier (no extra barrier)
+    int64_t srow[2];
+    unsigned sprev[2];
     if (P.D == 0) {
-        fwd_owner<T, THREADS, U, VEC, SHARD, SCALED>(p, P, blockIdx.x, sm, count, buf);
+        fwd_owner<T, THREADS, U, VEC, SHARD, SCALED, false>(p, P, blockIdx.x, sm, count, buf,
+                                                            srow, sprev);
     } else {
         // the static piece, then dynamic chunks; the next chunk's index is requested when
         // an owner starts, so the atomic's latency overlaps that owner's streaming
         unsigned next = 0u;
         if (tid == 0) next = atomicAdd(p.ws_dyn, 1u);
-        int64_t owner = blockIdx.x;
+        fwd_owner<T, THREADS, U, VEC, SHARD, SCALED, false>(p, P, blockIdx.x, sm, count, buf,
+                                                            srow, sprev);
+        int64_t owner = -1;
         int nb = 0;
         while (true) {
-            fwd_owner<T, THREADS, U, VEC, SHARD, SCALED>(p, P, owner, sm, count, buf);
+            if (owner >= 0) {
+                int64_t drow[2];
+                unsigned dprev[2];
+                fwd_owner<T, THREADS, U, VEC, SHARD, SCALED, true>(p, P, owner, sm, count, buf,
+                                                                   drow, dprev);
+            }
             if (tid == 0) sm.next_chunk[nb] = next;
             group_sync<THREADS, BAR>();
             const unsigned o = sm.next_chunk[nb];
@@ -630,7 +656,12 @@ __global__ void __launch_bounds__(THREADS, K1_FWD_MINB) k1_fwd_kernel(FwdParams 
             p.ws_dyn[1] = 0u;
         }
     }
-    fwd_flush_rows<T, THREADS, BAR, SHARD>(p, sm, count);
+    if (tid == 0) {
+        sm.split_prev[0] = sprev[0];
+        sm.split_prev[1] = sprev[1];
+    }
+    fwd_flush_rows<T, THREADS, BAR, SHARD>(p, sm, count);  // its barrier publishes split_prev
+    fwd_merge_owner_rows<T, THREADS, SHARD>(p, P, srow, sm);
 }
 
 // ---------------------------------------------------------------------------------
