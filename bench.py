@@ -339,6 +339,86 @@ def reference_arm(args, cfg, rank, world):
     print(json.dumps(out), flush=True)
 
 
+def reference_grpo_arm(args, cfg, rank, world):
+    """The GRPO loss block of grpo_arm run the reference trainer's way with the reference's
+    own K1 kernels (rebuilt for sm_100a by oracle/build_ref.py): slice the completion window,
+    divide it in place by the temperature, one K1 call per sequence (trainer.py:96-127,
+    through the reference's autograd wrapper, ops.py:49-89), then autograd back to the
+    logits.  Same workload, metric and algorithmic bytes as `--mode grpo`."""
+    if rank != 0:
+        return
+    from oracle import reference_k1
+    fn = reference_k1.autograd_function() if torch.cuda.is_available() else None
+    if fn is None:
+        print(json.dumps({"impl": "reference", "unavailable":
+                          "reference K1 build (oracle/_ref) or GPU absent"}), flush=True)
+        return
+    if not cfg["window"]:
+        cfg = CONFIGS["c3"]
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    B, S, V, dt = cfg["B"], cfg["S"], cfg["V"], cfg["dtype"]
+    T = 0.7
+    esize = torch.tensor([], dtype=dt).element_size()
+    window, targets, g_lp, g_h = make_workload(cfg, device, seed=4321)
+    parent = torch.as_strided(window, (B, S + 1, V), ((S + 1) * V, V, 1), 0)
+    N = B * S
+    fwd_bytes = N * V * esize + N * 20
+    bwd_bytes = N * V * esize + B * (S + 1) * V * esize + N * 16
+    stream = torch.cuda.current_stream(device)
+
+    def step(timed_events=None):
+        x = parent.detach().requires_grad_(True)
+        logits = x.clone()  # the model output the trainer receives
+        if timed_events:
+            timed_events[0].record(stream)
+        w = logits[:, :-1, :][:, -S:, :]
+        w.div_(T)
+        lps, ents = [], []
+        for b in range(B):
+            lp, h, _ = fn.apply(w[b].contiguous(), targets[b].contiguous())
+            lps.append(lp.unsqueeze(0))
+            ents.append(h.unsqueeze(0))
+        lp, h = torch.cat(lps), torch.cat(ents)
+        if timed_events:
+            timed_events[1].record(stream)
+        (d,) = torch.autograd.grad((lp, h), x, (g_lp, g_h))
+        if timed_events:
+            timed_events[2].record(stream)
+        return d
+
+    for _ in range(max(3, args.warmup)):
+        step()
+    torch.cuda.synchronize(device)
+    K = args.steps
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(K)]
+    for i in range(K):
+        step(ev[i])
+    torch.cuda.synchronize(device)
+    f_ms = statistics.mean(e[0].elapsed_time(e[1]) for e in ev)
+    b_ms = statistics.mean(e[1].elapsed_time(e[2]) for e in ev)
+    total = f_ms + b_ms
+    value = (fwd_bytes + bwd_bytes) / (total / 1e3) / 1e9
+    out = {
+        "metric": METRIC, "value": round(value, 2), "unit": UNIT, "impl": "reference",
+        "n_gpus": world, "steps": K, "warmup": max(3, args.warmup),
+        "ms_per_step": round(total, 4), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": DTYPE_NAME[dt], "data": "synthetic",
+        "rows_per_s": round(N / (total / 1e3), 1),
+        "config": {"workload": "GRPO loss block on " + cfg["workload"], "global_batch": B,
+                   "seq_len": S, "vocab": V, "temperature": T,
+                   "parallelism": "one GPU, the reference trainer's per-sequence loop"},
+        "reference_trainer_sm100a": {"fwd_ms": round(f_ms, 4), "bwd_ms": round(b_ms, 4),
+                                     "kernel_launches_per_step": 2 * B,
+                                     "note": "reference kernels rebuilt for sm_100a "
+                                             "(oracle/build_ref.py) in the reference "
+                                             "trainer's sequence; CUDA events"},
+        "e2e": {"value": round(value, 2), "unit": UNIT, "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(out), flush=True)
+
+
 def time_reference_k1_gpu(cfg, iters=20):
     """The reference's own CUDA K1 (csrc/fused_logprob.cu, rebuilt for sm_100a by
     oracle/build_ref.py) on the same workload shape, timed with CUDA events (median).
@@ -939,7 +1019,10 @@ def main():
     rank, local_rank, world = dist_env()
     cfg = CONFIGS[args.config]
     if args.impl == "reference":
-        reference_arm(args, cfg, rank, world)
+        if args.mode == "grpo":
+            reference_grpo_arm(args, cfg, rank, world)
+        else:
+            reference_arm(args, cfg, rank, world)
     elif args.mode == "grpo":
         grpo_arm(args, cfg, rank, local_rank, world)
     elif args.mode == "lmhead":

@@ -49,3 +49,32 @@ def backward(logits, targets, lse, entropy, g_logp, g_ent, g_lse):
                                         g_logp.contiguous(), g_ent.contiguous(),
                                         g_lse.contiguous(), d)
     return d
+
+
+def autograd_function():
+    """torch.autograd.Function over the reference kernels, following the reference's own
+    wrapper (python/kernel_opt/ops.py:49-89): forward saves (logits, targets, lse,
+    entropy); backward replaces missing upstream gradients by zero tensors, allocates
+    d_logits with empty_like and calls the reference backward kernel.  Returns None when
+    the build is absent."""
+    import torch
+    if load() is None:
+        return None
+
+    class RefFusedLogprobEntropy(torch.autograd.Function):
+        @staticmethod
+        def forward(ctx, logits, targets):
+            lp, h, l = forward(logits, targets)
+            ctx.save_for_backward(logits, targets, l, h)
+            return lp, h, l
+
+        @staticmethod
+        def backward(ctx, g_logp, g_ent, g_lse):
+            logits, targets, l, h = ctx.saved_tensors
+            z = torch.zeros_like(l)
+            g_logp = z if g_logp is None else g_logp.float().contiguous()
+            g_ent = z if g_ent is None else g_ent.float().contiguous()
+            g_lse = z if g_lse is None else g_lse.float().contiguous()
+            return backward(logits, targets, l, h, g_logp, g_ent, g_lse), None
+
+    return RefFusedLogprobEntropy
