@@ -301,14 +301,19 @@ int launch_forward(const char* fn, const void* logits, const Rows& L, int64_t co
         p.dyn_units = csize;
     };
     int64_t grid = 1;
-    if (vec && kRingFwd && !SCALED) {
-        auto kern = k1::k1_fwd_ring_kernel<T, kRingWarps, kRingStages, kRingBytes, SHARD>;
-        const int threads = (kRingWarps + 1) * 32;
-        const size_t smem = (size_t)kRingStages * kRingBytes;
-        rc = grid_for(kern, dev, p.total, kMinUnitsPerBlockVec, &grid, threads, smem);
-        if (rc) return rc;
-        launch(kern, grid, threads, smem, stream, p);
-    } else if (vec) {
+    // (build-time alternatives are only instantiated when selected)
+    if constexpr (kRingFwd && !SCALED) {
+        if (vec) {
+            auto kern = k1::k1_fwd_ring_kernel<T, kRingWarps, kRingStages, kRingBytes, SHARD>;
+            const int threads = (kRingWarps + 1) * 32;
+            const size_t smem = (size_t)kRingStages * kRingBytes;
+            rc = grid_for(kern, dev, p.total, kMinUnitsPerBlockVec, &grid, threads, smem);
+            if (rc) return rc;
+            launch(kern, grid, threads, smem, stream, p);
+            return check_launch(fn);
+        }
+    }
+    if (vec) {
         auto kern = k1::k1_fwd_kernel<T, kFwdThreads, kUnroll, true, SHARD, SCALED>;
         rc = grid_for(kern, dev, p.total, kMinUnitsPerBlockVec, &grid, kFwdThreads);
         if (rc) return rc;
@@ -352,19 +357,27 @@ int launch_backward(const char* fn, const void* logits, const Rows& L, const Row
     p.g_lse = g_lse;
     p.scale = SCALED ? scale : 1.f;
     int64_t grid = 1;
-    if (vec && kRing) {
-        auto kern = k1::k1_bwd_ring_kernel<T, kRingWarps, kRingStages, kRingBytes, SCALED>;
-        const int threads = (kRingWarps + 1) * 32;
-        const size_t smem = (size_t)kRingStages * kRingBytes;
-        rc = grid_for(kern, dev, p.total, kMinUnitsPerBlockVec, &grid, threads, smem);
-        if (rc) return rc;
-        launch(kern, grid, threads, smem, stream, p);
-    } else if (vec) {
-        auto kern = k1::k1_bwd_kernel<T, kThreads, kUnrollBwd, true, SCALED>;
-        rc = grid_for(kern, dev, p.total, kMinUnitsPerBlockVec, &grid);
-        if (rc) return rc;
-        launch(kern, grid, kThreads, 0, stream, p);
+    // (build-time alternatives are only instantiated when selected)
+    if constexpr (kRing) {
+        if (vec) {
+            auto kern = k1::k1_bwd_ring_kernel<T, kRingWarps, kRingStages, kRingBytes, SCALED>;
+            const int threads = (kRingWarps + 1) * 32;
+            const size_t smem = (size_t)kRingStages * kRingBytes;
+            rc = grid_for(kern, dev, p.total, kMinUnitsPerBlockVec, &grid, threads, smem);
+            if (rc) return rc;
+            launch(kern, grid, threads, smem, stream, p);
+            return check_launch(fn);
+        }
     } else {
+        if (vec) {
+            auto kern = k1::k1_bwd_kernel<T, kThreads, kUnrollBwd, true, SCALED>;
+            rc = grid_for(kern, dev, p.total, kMinUnitsPerBlockVec, &grid);
+            if (rc) return rc;
+            launch(kern, grid, kThreads, 0, stream, p);
+            return check_launch(fn);
+        }
+    }
+    {
         auto kern = k1::k1_bwd_kernel<T, kThreads, kUnrollBwd, false, SCALED>;
         rc = grid_for(kern, dev, p.total, kMinUnitsPerBlockScalar, &grid);
         if (rc) return rc;
