@@ -113,6 +113,25 @@ constexpr int kMaxBlocksPerSm = 8;   // grid cap
 #define K1_FWD_TAIL_MIN_ROWS 4
 #endif
 constexpr int kMaxOwnersPerSm = 32;  // static pieces + dynamic chunks; sizes the workspace
+// Forward row groups (k1_fwd_rows_kernel): the smallest group of 1, 2 or 4 warps that gets
+// at least K1_FWD_ROWS_MIN whole rows from the queue; else whole-block groups when each
+// block gets at least K1_FWD_ROWS_BLOCK_MIN rows; else the block kernel, which splits rows
+// between blocks (and takes the scalar path).  Measured on B200 (forward, bf16, us, block
+// kernel -> row groups): 1024 x 152064 71.8 -> 67.9, 2048 x 152064 124.9 -> 110.9,
+// 16384 x 151936 809 -> 766, 32768 x 32000 446 -> 354, 65536 x 4096 362 -> 111.
+// 0 disables.
+#ifndef K1_FWD_ROWS
+#define K1_FWD_ROWS 1
+#endif
+#ifndef K1_FWD_ROWS_MIN
+#define K1_FWD_ROWS_MIN 3
+#endif
+#ifndef K1_FWD_ROWS_BLOCK_MIN
+#define K1_FWD_ROWS_BLOCK_MIN 2
+#endif
+#ifndef K1_FWD_ROWS_FORCE_GT
+#define K1_FWD_ROWS_FORCE_GT 0  // measurement builds only: always use this group size
+#endif
 constexpr int64_t kMinUnitsPerBlockVec = (int64_t)kThreads * kUnroll;
 constexpr int64_t kMinUnitsPerBlockScalar = (int64_t)kThreads * 64;
 
@@ -312,6 +331,30 @@ int launch_forward(const char* fn, const void* logits, const Rows& L, int64_t co
             launch(kern, grid, threads, smem, stream, p);
             return check_launch(fn);
         }
+    }
+    if (vec && K1_FWD_ROWS) {
+        // row groups: the smallest group that still gets K1_FWD_ROWS_MIN rows
+        auto rows_launch = [&](auto kern, int gt, int min_rows) -> int {
+            int64_t g = 1;
+            int r = grid_for(kern, dev, p.total, 1, &g, 256);
+            if (r) return r;
+            const int64_t groups = g * (256 / gt);
+            if (K1_FWD_ROWS_FORCE_GT != 0) {
+                if (gt != K1_FWD_ROWS_FORCE_GT) return -1;
+            } else if (L.n_rows < (int64_t)min_rows * groups) {
+                return -1;
+            }
+            launch(kern, g, 256, 0, stream, p);
+            return check_launch(fn);
+        };
+        constexpr int kMin = K1_FWD_ROWS_MIN;
+        rc = rows_launch(k1::k1_fwd_rows_kernel<T, 32, kUnroll, SHARD, SCALED>, 32, kMin);
+        if (rc < 0) rc = rows_launch(k1::k1_fwd_rows_kernel<T, 64, kUnroll, SHARD, SCALED>, 64, kMin);
+        if (rc < 0) rc = rows_launch(k1::k1_fwd_rows_kernel<T, 128, kUnroll, SHARD, SCALED>, 128, kMin);
+        if (rc < 0)
+            rc = rows_launch(k1::k1_fwd_rows_kernel<T, 256, kUnroll, SHARD, SCALED>, 256,
+                             K1_FWD_ROWS_BLOCK_MIN);
+        if (rc >= 0) return rc;
     }
     if (vec) {
         auto kern = k1::k1_fwd_kernel<T, kFwdThreads, kUnroll, true, SHARD, SCALED>;

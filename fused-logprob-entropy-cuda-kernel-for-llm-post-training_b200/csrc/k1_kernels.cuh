@@ -450,8 +450,8 @@ __device__ __forceinline__ void fwd_flush_rows(const FwdParams& p, FwdSmem<THREA
     group_sync<THREADS, BAR>();
 }
 
-// Split row r (its vectors span blocks bf..bl): merge every block's published piece and
-// write the row.  Called by the block that drew the last ticket, after its own loop; one
+// Split row r (its units span owners bf..bl): merge every owner's published part and
+// write the row.  Called by the block whose owner drew the last ticket; one
 // warp does the work with shuffles (no block barrier), lane 0 issues the target-logit
 // load first so that its latency overlaps the loads of the pieces.
 template <typename T, bool SHARD>
@@ -662,6 +662,161 @@ __global__ void __launch_bounds__(THREADS, K1_FWD_MINB) k1_fwd_kernel(FwdParams 
     }
     fwd_flush_rows<T, THREADS, BAR, SHARD>(p, sm, count);  // its barrier publishes split_prev
     fwd_merge_owner_rows<T, THREADS, SHARD>(p, P, srow, sm);
+}
+
+// ---------------------------------------------------------------------------------
+// Forward, row groups (many rows of moderate width): each group of GT threads (one, two
+// or four warps) takes whole rows from a global queue (an atomic counter) and reduces
+// each row on its own -- warp shuffles, plus a named barrier per group when GT > 32 --
+// so rows are never split between owners and no block-wide barrier is taken.  Rows are
+// handed out in order and a row is computed the same way by any group, so results do
+// not depend on which group took it.  The next row's index is requested, and the row's
+// target logit loaded, while the current row streams.
+// ---------------------------------------------------------------------------------
+template <int GT>
+struct RowsSmem {
+    static constexpr int NW = GT / 32;
+    float wmax[2][NW];
+    int wbad[2][NW];
+    double wz[2][NW];
+    double wt[2][NW];
+};
+
+__device__ __forceinline__ void named_sync(int id, int threads) {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+
+// Merge the group's per-thread states of one row (relative to the row maximum).  Returns
+// false -- uniformly -- when some thread flagged `bad`; the caller re-streams clamped.
+template <int GT>
+__device__ __forceinline__ bool rows_merge(float m, double z, double t, bool empty, bool bad,
+                                           RowsSmem<GT>& sm, int bar_id, int wig, int buf,
+                                           RowPartial& out) {
+    constexpr int NW = GT / 32;
+    const int lane = threadIdx.x & 31;
+    float M = warp_max_nan(empty ? -INFINITY : m);
+    bool any_bad = __any_sync(0xffffffffu, bad);
+    if constexpr (NW > 1) {
+        if (lane == 0) {
+            sm.wmax[buf][wig] = M;
+            sm.wbad[buf][wig] = any_bad ? 1 : 0;
+        }
+        named_sync(bar_id, GT);
+        M = sm.wmax[buf][0];
+        int b = sm.wbad[buf][0];
+#pragma unroll
+        for (int i = 1; i < NW; ++i) {
+            M = fmax_nan(M, sm.wmax[buf][i]);
+            b |= sm.wbad[buf][i];
+        }
+        any_bad = b != 0;
+    }
+    if (any_bad) {
+        if constexpr (NW > 1) named_sync(bar_id, GT);  // flags read before the retry
+        return false;
+    }
+    double zc = 0.0, tc = 0.0;
+    if (!empty) {
+        const float dm = m - M;
+        const float sc = (dm == 0.f) ? 1.f : ex2(dm * kLog2e);
+        zc = (double)sc * z;
+        tc = (double)sc * (t + (double)dm * z);
+    }
+    zc = warp_sum(zc);
+    tc = warp_sum(tc);
+    if constexpr (NW > 1) {
+        if (lane == 0) {
+            sm.wz[buf][wig] = zc;
+            sm.wt[buf][wig] = tc;
+        }
+        named_sync(bar_id, GT);
+        zc = 0.0;
+        tc = 0.0;
+#pragma unroll
+        for (int i = 0; i < NW; ++i) {
+            zc += sm.wz[buf][i];
+            tc += sm.wt[buf][i];
+        }
+    }
+    out.z = zc;
+    out.t = tc;
+    out.m = M;
+    if (M == -INFINITY) out.z = out.t = 0.0;
+    out.pad = 0.f;
+    return true;
+}
+
+template <typename T, int GT, int U, bool SHARD, bool SCALED>
+__global__ void __launch_bounds__(256, K1_FWD_MINB) k1_fwd_rows_kernel(FwdParams p) {
+    constexpr int NG = 256 / GT;
+    __shared__ RowsSmem<GT> gsm[NG];
+    __shared__ int64_t gnext[NG][2];
+    pdl_wait();
+    pdl_trigger();
+    const int g = threadIdx.x / GT, gtid = threadIdx.x % GT, wig = gtid >> 5;
+    const int bar_id = 1 + g;
+    RowsSmem<GT>& sm = gsm[g];
+    const unsigned n_groups = gridDim.x * NG;
+    unsigned next = 0u;
+    if (gtid == 0) next = atomicAdd(p.ws_dyn, 1u);
+    int buf = 0, nb = 0;
+    while (true) {
+        // the group's next row (thread 0 of the group drew it)
+        int64_t r;
+        if constexpr (GT == 32) {
+            r = (int64_t)__shfl_sync(0xffffffffu, next, 0);
+        } else {
+            if (gtid == 0) gnext[g][nb] = (int64_t)next;
+            named_sync(bar_id, GT);
+            r = gnext[g][nb];
+            nb ^= 1;
+        }
+        if (r >= p.n_rows) break;
+        const T* rowp = reinterpret_cast<const T*>(p.logits) + p.lay.offset(r);
+        int64_t tg = -1;
+        if (gtid == 0) {
+            next = atomicAdd(p.ws_dyn, 1u);  // the row after this one
+            tg = p.targets[r];               // consumed after the row has streamed
+        }
+        float xt = 0.f;
+        bool has = false;
+        FwdState st;
+        RowPartial part;
+        for (int pass = 0; pass < 2; ++pass) {
+            st.init();
+            fwd_stream_vec<T, SCALED, GT, U>(rowp, 0, p.vpr, st, gtid, pass == 1, p.scale);
+            if (gtid == 0) {  // the target logit's load overlaps the merge
+                const int64_t tl = SHARD ? tg - p.col_offset : tg;
+                has = (tg >= 0) && (tl >= 0) && (tl < p.vocab);
+                xt = has ? target_logit<T>(rowp + tl, p.scale) : 0.f;
+            }
+            const bool ok = rows_merge<GT>(st.m, st.z64(), st.t64(), st.m <= DT<T>::kLowest,
+                                           pass == 0 && st.saw_neg_inf(), sm, bar_id, wig, buf,
+                                           part);
+            buf ^= 1;
+            if (ok) break;
+        }
+        if (gtid == 0) {
+            if constexpr (SHARD) {
+                k1_partial o;
+                o.z = part.z;
+                o.t = part.t;
+                o.m = part.m;
+                o.x_t = has ? xt : 0.f;
+                o.has_target = has ? 1 : 0;
+                o.reserved = 0;
+                p.partials[r] = o;
+            } else {
+                finalize_row(part, has ? (double)xt : 0.0, p.logprob + r, p.entropy + r,
+                             p.lse + r);
+            }
+        }
+    }
+    // the last group out leaves the counters zeroed for the next call
+    if (gtid == 0 && atomicAdd(p.ws_dyn + 1, 1u) == n_groups - 1) {
+        p.ws_dyn[0] = 0u;
+        p.ws_dyn[1] = 0u;
+    }
 }
 
 // ---------------------------------------------------------------------------------

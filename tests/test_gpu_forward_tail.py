@@ -1,9 +1,10 @@
-"""The forward's dynamic tail (launches with at least 4 rows per block): the last quarter
-of the rows goes out as whole-row chunks taken from an atomic counter, several rows per
-chunk once the workspace's owner slots would run out.  Results must meet the oracle's
-tolerances, be bit-identical from run to run (chunk boundaries are fixed; which block
-takes a chunk must not matter), leave the counters zeroed for the next call, and agree
-between the strided and contiguous layouts."""
+"""Forward work distribution.  Row groups (k1_fwd_rows_kernel: groups of 1, 2, 4 or 8
+warps taking whole rows from an atomic queue) serve launches with enough rows; the block
+kernel (rows split between blocks, with a dynamic tail of whole-row chunks from 4 rows per
+block) serves the rest and the scalar path.  Results must meet the oracle's tolerances, be
+bit-identical from run to run (which group or block takes a row or chunk must not
+matter), leave the queue counters zeroed for the next call, and agree between the strided
+and contiguous layouts."""
 import pytest
 import torch
 
@@ -12,13 +13,14 @@ from _gpu import check_forward_outputs, seeded_logits, seeded_targets
 
 pytestmark = pytest.mark.gpu
 
-# (rows, vocab, dtype): vector path with one- and multi-row tail chunks, fp32, fp16, and
-# the scalar path (a vocab whose rows are not 16-byte multiples)
+# (rows, vocab, dtype) on 148 SMs: row groups of several sizes, and the scalar path
+# (a vocab whose rows are not 16-byte multiples) through the block kernel with its tail
 SHAPES = [
-    (20000, 256, torch.bfloat16),    # ~64 rows per block: multi-row chunks (owner cap)
+    (20000, 256, torch.bfloat16),
     (3000, 4096, torch.float32),
     (2500, 2048, torch.float16),
-    (1777, 1003, torch.bfloat16),    # scalar path
+    (1777, 1003, torch.bfloat16),    # scalar path: block kernel, dynamic tail
+    (40000, 3001, torch.float32),    # scalar path: multi-row tail chunks (owner cap)
 ]
 
 
@@ -52,3 +54,59 @@ def test_tail_strided_window_equals_contiguous():
     b = kernel_opt.fused_logprob_entropy_forward(win.contiguous(), t)
     for u, v in zip(a, b):
         torch.testing.assert_close(u, v, rtol=0, atol=0)
+
+
+# Row groups: the smallest group of 1, 2 or 4 warps with >= 3 rows each, else 8-warp
+# groups with >= 2 rows each (444 blocks of 8 warps on 148 SMs); these shapes select each.
+ROW_GROUP_SHAPES = [
+    (60000, 512, torch.bfloat16),   # one-warp groups
+    (8000, 1024, torch.float16),    # two-warp groups
+    (4000, 4096, torch.float32),    # four-warp groups
+    (2000, 2048, torch.bfloat16),   # whole-block groups
+    (600, 8192, torch.bfloat16),    # block kernel (too few rows for groups)
+]
+
+
+@pytest.mark.parametrize("rows,vocab,dtype", ROW_GROUP_SHAPES)
+def test_row_groups_match_oracle_and_repeat(rows, vocab, dtype):
+    x = seeded_logits((rows, vocab), dtype, 3.0, seed=rows + 5)
+    t = seeded_targets((rows,), vocab, seed=rows + 6)
+    t[7] = -100
+    x.view(-1, vocab)[11, ::5] = float("-inf")  # the clamped re-stream inside a group
+    xg, tg = x.cuda(), t.cuda()
+    first = kernel_opt.fused_logprob_entropy_forward(xg, tg)
+    idx = torch.cat([torch.arange(0, 64), torch.arange(rows - 64, rows)])
+    check_forward_outputs(tuple(o[idx.cuda()] for o in first), x[idx], t[idx],
+                          f"row groups {rows}x{vocab} {dtype}")
+    for _ in range(2):
+        again = kernel_opt.fused_logprob_entropy_forward(xg, tg)
+        for a, b in zip(first, again):
+            torch.testing.assert_close(a, b, rtol=0, atol=0)
+
+
+def test_row_groups_scaled_and_shard():
+    from kernel_opt import _C, grpo
+    from oracle import oracle
+    rows, V = 60000, 512
+    x = seeded_logits((rows, V), torch.bfloat16, 3.0, seed=9).cuda()
+    t = seeded_targets((rows,), V, seed=10).cuda()
+    # temperature folded in == division first (same launch shape, same bits)
+    T = 0.85
+    a = [torch.empty(rows, device="cuda") for _ in range(3)]
+    b = [torch.empty(rows, device="cuda") for _ in range(3)]
+    _C.fused_logprob_entropy_scaled(x, t, *a, grpo.temperature_scale(T))
+    _C.fused_logprob_entropy_v1(x.clone().div_(T), t, *b)
+    for u, v in zip(a, b):
+        torch.testing.assert_close(u, v, rtol=0, atol=0)
+    # vocabulary shard partials against the oracle's restatement
+    off = 1000
+    parts = torch.empty((rows, 4), dtype=torch.float64, device="cuda")
+    tt = t + off
+    _C.vocab_shard_partials(x, tt, off, parts)
+    want = oracle.unpack_partials(oracle.shard_partials(x[:256].cpu(), tt[:256].cpu(), off))
+    got = oracle.unpack_partials(parts[:256].cpu().numpy())
+    import numpy as np
+    np.testing.assert_array_equal(got["has"], want["has"])
+    np.testing.assert_allclose(got["m"], want["m"], rtol=0, atol=0)
+    np.testing.assert_allclose(got["z"], want["z"], rtol=1e-5)
+    np.testing.assert_allclose(got["x_t"], want["x_t"], rtol=0, atol=0)
