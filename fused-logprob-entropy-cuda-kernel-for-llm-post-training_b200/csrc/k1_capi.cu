@@ -13,6 +13,7 @@
 #include <map>
 #include <mutex>
 #include <string>
+#include <type_traits>
 #include <utility>
 
 #include "k1_ring.cuh"
@@ -332,8 +333,9 @@ int launch_forward(const char* fn, const void* logits, const Rows& L, int64_t co
             return check_launch(fn);
         }
     }
-    if (vec && K1_FWD_ROWS) {
-        // row groups: the smallest group that still gets K1_FWD_ROWS_MIN rows
+    if (K1_FWD_ROWS) {
+        // row groups: the smallest group that still gets K1_FWD_ROWS_MIN rows (any
+        // alignment: rows that are not whole vectors are peeled, see fwd_stream_peeled)
         auto rows_launch = [&](auto kern, int gt, int min_rows) -> int {
             int64_t g = 1;
             int r = grid_for(kern, dev, p.total, 1, &g, 256);
@@ -347,13 +349,20 @@ int launch_forward(const char* fn, const void* logits, const Rows& L, int64_t co
             launch(kern, g, 256, 0, stream, p);
             return check_launch(fn);
         };
-        constexpr int kMin = K1_FWD_ROWS_MIN;
-        rc = rows_launch(k1::k1_fwd_rows_kernel<T, 32, kUnroll, SHARD, SCALED>, 32, kMin);
-        if (rc < 0) rc = rows_launch(k1::k1_fwd_rows_kernel<T, 64, kUnroll, SHARD, SCALED>, 64, kMin);
-        if (rc < 0) rc = rows_launch(k1::k1_fwd_rows_kernel<T, 128, kUnroll, SHARD, SCALED>, 128, kMin);
-        if (rc < 0)
-            rc = rows_launch(k1::k1_fwd_rows_kernel<T, 256, kUnroll, SHARD, SCALED>, 256,
-                             K1_FWD_ROWS_BLOCK_MIN);
+        auto try_all = [&](auto vec_tag) -> int {
+            constexpr bool V = decltype(vec_tag)::value;
+            constexpr int kMin = K1_FWD_ROWS_MIN;
+            int r = rows_launch(k1::k1_fwd_rows_kernel<T, 32, kUnroll, V, SHARD, SCALED>, 32, kMin);
+            if (r < 0)
+                r = rows_launch(k1::k1_fwd_rows_kernel<T, 64, kUnroll, V, SHARD, SCALED>, 64, kMin);
+            if (r < 0)
+                r = rows_launch(k1::k1_fwd_rows_kernel<T, 128, kUnroll, V, SHARD, SCALED>, 128, kMin);
+            if (r < 0)
+                r = rows_launch(k1::k1_fwd_rows_kernel<T, 256, kUnroll, V, SHARD, SCALED>, 256,
+                                K1_FWD_ROWS_BLOCK_MIN);
+            return r;
+        };
+        rc = vec ? try_all(std::true_type{}) : try_all(std::false_type{});
         if (rc >= 0) return rc;
     }
     if (vec) {

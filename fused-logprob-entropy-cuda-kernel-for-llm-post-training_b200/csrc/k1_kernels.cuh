@@ -314,32 +314,41 @@ __device__ __forceinline__ void fwd_stream_vec(const T* rowp, int64_t j0, int64_
     if (j < j1) fwd_remainder<T, SCALED, THREADS, U>(vp, j, j1, st, clamp, s);
 }
 
-// Stream elements [j0, j1) of one row (scalar path: any alignment).
-template <typename T, bool SCALED, int THREADS>
-__device__ __forceinline__ void fwd_stream_scalar(const T* rowp, int64_t j0, int64_t j1,
-                                                  FwdState& st, float s) {
+// Rows whose start is not 16-byte aligned (a vocabulary that is not a whole number of
+// vectors, or such a row stride): a segment [j0, j1) is peeled into a head of single
+// elements up to the first 16-byte boundary, an aligned interior of vectors and a tail of
+// single elements.  Returns the interior [a0, a1) (a0 = a1 when there is none).
+template <typename T>
+__device__ __forceinline__ void peel(const T* rowp, int64_t j0, int64_t j1, int64_t& a0,
+                                     int64_t& a1) {
+    constexpr int EPV = DT<T>::kEPV;
+    const uintptr_t a = reinterpret_cast<uintptr_t>(rowp + j0);
+    const int64_t head = min((int64_t)(((16u - (unsigned)(a & 15u)) & 15u) / sizeof(T)), j1 - j0);
+    a0 = j0 + head;
+    a1 = a0 + (j1 - a0) / EPV * EPV;
+}
+
+// Stream elements [j0, j1) of one row at any alignment: the aligned interior through the
+// vector path, the (at most 2 * (EPV - 1)) head and tail elements one per thread, each
+// folded in as a pair with padding (the padding adds e = 0 like any masked element).
+// Single elements are always clamped; `clamp` applies to the interior as on the vector path.
+template <typename T, bool SCALED, int THREADS, int U>
+__device__ __forceinline__ void fwd_stream_peeled(const T* rowp, int64_t j0, int64_t j1,
+                                                  FwdState& st, int tid, bool clamp, float s) {
     using D = DT<T>;
-    constexpr int U = 8;
-    for (int64_t j = j0 + threadIdx.x; j < j1; j += (int64_t)U * THREADS) {
-        float f[U];
-#pragma unroll
-        for (int u = 0; u < U; ++u) {
-            int64_t jj = j + (int64_t)u * THREADS;
-            if (jj < j1) {
-                const float x = D::load1(rowp + jj);
-                f[u] = D::clamp1(SCALED ? scale1<T>(x, s) : x);
-            } else {
-                f[u] = D::kLowest;
-            }
-        }
-        float mx = f[0];
-#pragma unroll
-        for (int u = 1; u < U; ++u) mx = fmax_nan(mx, f[u]);
-        st.rescale(mx);
-        const float2 nm = splat(-st.m);
-#pragma unroll
-        for (int i = 0; i < U / 2; ++i) st.accum(make_float2(f[2 * i], f[2 * i + 1]), nm);
-        st.np += (float)(U / 2);
+    int64_t a0, a1;
+    peel(rowp, j0, j1, a0, a1);
+    if (a1 > a0)
+        fwd_stream_vec<T, SCALED, THREADS, U>(rowp + a0, 0, (a1 - a0) / D::kEPV, st, tid, clamp,
+                                              s);
+    const int64_t nh = a0 - j0, ne = nh + (j1 - a1);
+    if (tid < ne) {
+        const int64_t e = tid < nh ? j0 + tid : a1 + (tid - nh);
+        const float x = D::load1(rowp + e);
+        const float xv = D::clamp1(SCALED ? scale1<T>(x, s) : x);
+        st.rescale(xv);
+        st.accum(make_float2(xv, D::kLowest), splat(-st.m));
+        st.np += 1.f;
     }
 }
 
@@ -568,10 +577,15 @@ __device__ __forceinline__ void fwd_owner(const FwdParams& p, const Partition& P
                     break;
             }
         } else {
-            st.init();
-            fwd_stream_scalar<T, SCALED, THREADS>(rowp, j0, j1, st, p.scale);
-            seg_merge<THREADS, BAR>(st.m, st.z64(), st.t64(), st.m <= DT<T>::kLowest, false, sm,
-                                    buf, part);
+            for (int pass = 0; pass < 2; ++pass) {
+                st.init();
+                // 4 vectors a thread per chunk: this kernel is at its register budget
+                fwd_stream_peeled<T, SCALED, THREADS, 4>(rowp, j0, j1, st, tid, pass == 1,
+                                                         p.scale);
+                if (seg_merge<THREADS, BAR>(st.m, st.z64(), st.t64(), st.m <= DT<T>::kLowest,
+                                            pass == 0 && st.saw_neg_inf(), sm, buf, part))
+                    break;
+            }
         }
         buf ^= 1;
         if (j0 == 0 && j1 == p.vpr) {
@@ -746,7 +760,7 @@ __device__ __forceinline__ bool rows_merge(float m, double z, double t, bool emp
     return true;
 }
 
-template <typename T, int GT, int U, bool SHARD, bool SCALED>
+template <typename T, int GT, int U, bool VEC, bool SHARD, bool SCALED>
 __global__ void __launch_bounds__(256, K1_FWD_MINB) k1_fwd_rows_kernel(FwdParams p) {
     constexpr int NG = 256 / GT;
     __shared__ RowsSmem<GT> gsm[NG];
@@ -784,7 +798,10 @@ __global__ void __launch_bounds__(256, K1_FWD_MINB) k1_fwd_rows_kernel(FwdParams
         RowPartial part;
         for (int pass = 0; pass < 2; ++pass) {
             st.init();
-            fwd_stream_vec<T, SCALED, GT, U>(rowp, 0, p.vpr, st, gtid, pass == 1, p.scale);
+            if constexpr (VEC)
+                fwd_stream_vec<T, SCALED, GT, U>(rowp, 0, p.vpr, st, gtid, pass == 1, p.scale);
+            else
+                fwd_stream_peeled<T, SCALED, GT, U>(rowp, 0, p.vpr, st, gtid, pass == 1, p.scale);
             if (gtid == 0) {  // the target logit's load overlaps the merge
                 const int64_t tl = SHARD ? tg - p.col_offset : tg;
                 has = (tg >= 0) && (tl >= 0) && (tl < p.vocab);
@@ -907,10 +924,69 @@ __device__ __forceinline__ uint4 vec_set(uint4 o, int k, float val) {
     return make_uint4(w[0], w[1], w[2], w[3]);
 }
 
+// Gradient of vectors [j0, j1) of a row through a 16-byte aligned vector base xv / dv.
+// tl_rel is the target column relative to the base's first element (outside [0, vectors
+// x EPV) when the target is elsewhere); xr is the row's first element.
+template <typename T, bool SCALED, int THREADS, int U>
+__device__ __forceinline__ void bwd_stream_vec(const uint4* xv, uint4* dv, int64_t j0, int64_t j1,
+                                               const BwdRow& q, int64_t tl_rel, const T* xr,
+                                               float s) {
+    constexpr int EPV = DT<T>::kEPV;
+    constexpr int64_t kSpan = (int64_t)(U - 1) * THREADS;
+    constexpr int64_t kStep = (int64_t)U * THREADS;
+    int64_t j = j0 + threadIdx.x;
+    for (; j + kSpan < j1; j += kStep) {
+        uint4 v[U];
+        load_vectors<U, THREADS>(v, xv, j);
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            const int64_t jj = j + (int64_t)u * THREADS;
+            uint4 o = bwd_vector<T, SCALED>(v[u], q, s);
+            const uint64_t k = (uint64_t)(tl_rel - jj * EPV);
+            if (k < (uint64_t)EPV) o = vec_set<T>(o, (int)k, bwd_target_out<T>(xr, q, s));
+            stg_stream(dv + jj, o);
+        }
+    }
+    if (j < j1) {  // remainder: one predicated chunk
+        uint4 v[U];
+        load_vectors_masked<T, U, THREADS>(v, xv, j, j1);
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            const int64_t jj = j + (int64_t)u * THREADS;
+            if (jj < j1) {
+                uint4 o = bwd_vector<T, SCALED>(v[u], q, s);
+                const uint64_t k = (uint64_t)(tl_rel - jj * EPV);
+                if (k < (uint64_t)EPV) o = vec_set<T>(o, (int)k, bwd_target_out<T>(xr, q, s));
+                stg_stream(dv + jj, o);
+            }
+        }
+    }
+}
+
+// Gradient of the single element j of a row: the packed path's operations one lane at a
+// time, so both paths produce identical bits.
+template <typename T, bool SCALED>
+__device__ __forceinline__ void bwd_element(const T* xr, T* dr, int64_t j, const BwdRow& q,
+                                            float s) {
+    using D = DT<T>;
+    float g;
+    if (j == q.tl) {
+        g = bwd_target_out<T>(xr, q, s);
+    } else {
+        const float xraw = D::load1(xr + j);
+        const float x = D::clamp1(SCALED ? scale1<T>(xraw, s) : xraw);
+        const float d = __fadd_rn(x, -q.lse);
+        const float pp = ex2(__fmul_rn(d, kLog2e));
+        g = __fmaf_rn(-q.ge, __fmul_rn(pp, d), __fmul_rn(pp, q.c0));
+        if constexpr (SCALED) g = scale1<T>(D::round1(g), s);
+    }
+    D::store1(dr + j, g);
+}
+
 template <typename T, int THREADS, int U, bool VEC, bool SCALED = false>
 __global__ void __launch_bounds__(THREADS, K1_BWD_MINB) k1_bwd_kernel(BwdParams p) {
     using D = DT<T>;
-    constexpr int EPV = VEC ? D::kEPV : 1;
+    constexpr int EPV = D::kEPV;
     pdl_wait();
     pdl_trigger();
     const int64_t G = gridDim.x, b = blockIdx.x;
@@ -936,58 +1012,25 @@ __global__ void __launch_bounds__(THREADS, K1_BWD_MINB) k1_bwd_kernel(BwdParams 
             q.tl = (tg >= 0 && tl >= 0 && tl < p.vocab) ? tl : -1;
         }
         if constexpr (VEC) {
-            const uint4* xv = reinterpret_cast<const uint4*>(xr);
-            uint4* dv = reinterpret_cast<uint4*>(dr);
-            constexpr int64_t kSpan = (int64_t)(U - 1) * THREADS;
-            constexpr int64_t kStep = (int64_t)U * THREADS;
-            int64_t j = j0 + threadIdx.x;
-            auto emit = [&](const uint4(&v)[U], int64_t jb) {
-#pragma unroll
-                for (int u = 0; u < U; ++u) {
-                    const int64_t jj = jb + (int64_t)u * THREADS;
-                    uint4 o = bwd_vector<T, SCALED>(v[u], q, p.scale);
-                    const uint64_t k = (uint64_t)(q.tl - jj * EPV);
-                    if (k < (uint64_t)EPV) o = vec_set<T>(o, (int)k, bwd_target_out<T>(xr, q, p.scale));
-                    stg_stream(dv + jj, o);
-                }
-            };
-            for (; j + kSpan < j1; j += kStep) {
-                uint4 v[U];
-                load_vectors<U, THREADS>(v, xv, j);
-                emit(v, j);
-            }
-            if (j < j1) {  // remainder: one predicated chunk
-                uint4 v[U];
-                load_vectors_masked<T, U, THREADS>(v, xv, j, j1);
-#pragma unroll
-                for (int u = 0; u < U; ++u) {
-                    const int64_t jj = j + (int64_t)u * THREADS;
-                    if (jj < j1) {
-                        uint4 o = bwd_vector<T, SCALED>(v[u], q, p.scale);
-                        const uint64_t k = (uint64_t)(q.tl - jj * EPV);
-                        if (k < (uint64_t)EPV)
-                            o = vec_set<T>(o, (int)k, bwd_target_out<T>(xr, q, p.scale));
-                        stg_stream(dv + jj, o);
-                    }
-                }
-            }
+            bwd_stream_vec<T, SCALED, THREADS, U>(reinterpret_cast<const uint4*>(xr),
+                                                  reinterpret_cast<uint4*>(dr), j0, j1, q, q.tl,
+                                                  xr, p.scale);
         } else {
-            for (int64_t j = j0 + threadIdx.x; j < j1; j += THREADS) {
-                float g;
-                if (j == q.tl) {
-                    g = bwd_target_out<T>(xr, q, p.scale);
-                } else {
-                    // the packed path's operations one lane at a time, so both paths
-                    // produce identical bits
-                    const float xraw = D::load1(xr + j);
-                    const float x = D::clamp1(SCALED ? scale1<T>(xraw, p.scale) : xraw);
-                    const float d = __fadd_rn(x, -q.lse);
-                    const float pp = ex2(__fmul_rn(d, kLog2e));
-                    g = __fmaf_rn(-q.ge, __fmul_rn(pp, d), __fmul_rn(pp, q.c0));
-                    if constexpr (SCALED) g = scale1<T>(D::round1(g), p.scale);
-                }
-                D::store1(dr + j, g);
-            }
+            // Rows that are not whole vectors: when the logits row and the gradient row
+            // share their 16-byte misalignment, the aligned interior goes through the vector
+            // path and only the head and tail elements one at a time; otherwise every
+            // element one at a time.
+            int64_t a0 = j1, a1 = j1;
+            const uintptr_t ax = reinterpret_cast<uintptr_t>(xr + j0);
+            const uintptr_t ad = reinterpret_cast<uintptr_t>(dr + j0);
+            if (((ax ^ ad) & 15u) == 0) peel(xr, j0, j1, a0, a1);
+            if (a1 > a0)
+                bwd_stream_vec<T, SCALED, THREADS, 4>(reinterpret_cast<const uint4*>(xr + a0),
+                                                      reinterpret_cast<uint4*>(dr + a0), 0,
+                                                      (a1 - a0) / EPV, q, q.tl - a0, xr, p.scale);
+            const int64_t nh = a0 - j0, ne = nh + (j1 - a1);
+            for (int64_t e = threadIdx.x; e < ne; e += THREADS)
+                bwd_element<T, SCALED>(xr, dr, e < nh ? j0 + e : a1 + (e - nh), q, p.scale);
         }
         start += j1 - j0;
         ++r;

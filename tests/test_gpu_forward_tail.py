@@ -110,3 +110,39 @@ def test_row_groups_scaled_and_shard():
     np.testing.assert_allclose(got["m"], want["m"], rtol=0, atol=0)
     np.testing.assert_allclose(got["z"], want["z"], rtol=1e-5)
     np.testing.assert_allclose(got["x_t"], want["x_t"], rtol=0, atol=0)
+
+
+# Vocabularies that are not whole 16-byte vectors (GPT-2's 50257, odd shard widths): rows
+# are peeled into single-element head and tail around an aligned vector interior.
+PEELED = [
+    (12000, 50257, torch.bfloat16),   # row groups, one-warp groups
+    (1500, 50257, torch.float16),     # row groups, whole-block groups
+    (300, 32001, torch.bfloat16),     # block kernel (rows split between blocks)
+    (2000, 12347, torch.float32),
+]
+
+
+@pytest.mark.parametrize("rows,vocab,dtype", PEELED)
+def test_peeled_rows_forward_and_backward(rows, vocab, dtype):
+    from _gpu import check_grad, grads_like
+    from kernel_opt import _C
+    x = seeded_logits((rows, vocab), dtype, 3.0, seed=vocab)
+    t = seeded_targets((rows,), vocab, seed=vocab + 1)
+    t[0], t[1], t[2] = 0, vocab - 1, -100   # targets in the head / tail elements
+    x.view(-1, vocab)[3, 1::7] = float("-inf")
+    xg, tg = x.cuda(), t.cuda()
+    outs = kernel_opt.fused_logprob_entropy_forward(xg, tg)
+    idx = torch.cat([torch.arange(0, 48), torch.arange(rows - 48, rows)])
+    fwd = check_forward_outputs(tuple(o[idx.cuda()] for o in outs), x[idx], t[idx],
+                                f"peeled {rows}x{vocab} {dtype}")
+    g = grads_like((rows,), seed=vocab + 2)
+    lp, h, l = outs
+    d = torch.empty_like(xg)
+    _C.fused_logprob_entropy_v1_backward(xg, tg, l, h, *(a.cuda() for a in g), d)
+    sub = idx[:16]
+    check_grad(d[sub.cuda()], x[sub], t[sub], *(a[sub] for a in g), what="peeled bwd",
+               fwd=tuple(a[:16] for a in fwd))
+    # in place: same bits as out of place (the backward is elementwise)
+    d2 = xg.clone()
+    _C.fused_logprob_entropy_v1_backward(d2, tg, l, h, *(a.cuda() for a in g), d2)
+    torch.testing.assert_close(d2, d, rtol=0, atol=0)
