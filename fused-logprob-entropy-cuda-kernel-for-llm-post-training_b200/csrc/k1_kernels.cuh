@@ -142,7 +142,10 @@ __device__ __forceinline__ float target_logit(const T* p, float s) {
 #define K1_FWD_MINB 3
 #endif
 #ifndef K1_BWD_MINB
-#define K1_BWD_MINB 4
+#define K1_BWD_MINB 3
+#endif
+#ifndef K1_BWD_PEEL_UNROLL
+#define K1_BWD_PEEL_UNROLL 4  // vectors a thread per chunk on peeled (misaligned) rows
 #endif
 #ifndef K1_MIXED_ADD
 #define K1_MIXED_ADD 1
@@ -1025,7 +1028,7 @@ __global__ void __launch_bounds__(THREADS, K1_BWD_MINB) k1_bwd_kernel(BwdParams 
             const uintptr_t ad = reinterpret_cast<uintptr_t>(dr + j0);
             if (((ax ^ ad) & 15u) == 0) peel(xr, j0, j1, a0, a1);
             if (a1 > a0)
-                bwd_stream_vec<T, SCALED, THREADS, 4>(reinterpret_cast<const uint4*>(xr + a0),
+                bwd_stream_vec<T, SCALED, THREADS, K1_BWD_PEEL_UNROLL>(reinterpret_cast<const uint4*>(xr + a0),
                                                       reinterpret_cast<uint4*>(dr + a0), 0,
                                                       (a1 - a0) / EPV, q, q.tl - a0, xr, p.scale);
             const int64_t nh = a0 - j0, ne = nh + (j1 - a1);
