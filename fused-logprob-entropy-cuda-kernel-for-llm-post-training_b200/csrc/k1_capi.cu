@@ -216,6 +216,18 @@ bool vector_ok(const void* base, int es, const Rows& L) {
     return true;
 }
 
+// Whether every logits row and its gradient row have the same address modulo 16 bytes
+// (then both can be peeled at the same element: see peel in k1_kernels.cuh).
+bool peel_congruent(const void* x, const void* d, int es, const Rows& L, const Rows& D) {
+    const int64_t base = (int64_t)(reinterpret_cast<uintptr_t>(x) % 16) -
+                         (int64_t)(reinterpret_cast<uintptr_t>(d) % 16);
+    if (base != 0) return false;
+    if (L.inner_rows > 1 && ((L.inner_stride - D.inner_stride) * es) % 16 != 0) return false;
+    if (L.n_rows > L.inner_rows && ((L.outer_stride - D.outer_stride) * es) % 16 != 0)
+        return false;
+    return true;
+}
+
 k1::RowLayout layout_of(const Rows& L) {
     k1::RowLayout r;
     r.inner_rows = L.inner_rows;
@@ -416,6 +428,17 @@ int launch_backward(const char* fn, const void* logits, const Rows& L, const Row
             const int threads = (kRingWarps + 1) * 32;
             const size_t smem = (size_t)kRingStages * kRingBytes;
             rc = grid_for(kern, dev, p.total, kMinUnitsPerBlockVec, &grid, threads, smem);
+            if (rc) return rc;
+            launch(kern, grid, threads, smem, stream, p);
+            return check_launch(fn);
+        }
+        if (peel_congruent(logits, d_logits, es, L, D)) {
+            // rows that are not whole vectors: the ring over each segment's aligned interior
+            auto kern = k1::k1_bwd_ring_kernel<T, kRingWarps, kRingStages, kRingBytes, SCALED, true>;
+            const int threads = (kRingWarps + 1) * 32;
+            const size_t smem = (size_t)kRingStages * kRingBytes;
+            rc = grid_for(kern, dev, p.total, kMinUnitsPerBlockVec * k1::DT<T>::kEPV, &grid,
+                          threads, smem);
             if (rc) return rc;
             launch(kern, grid, threads, smem, stream, p);
             return check_launch(fn);

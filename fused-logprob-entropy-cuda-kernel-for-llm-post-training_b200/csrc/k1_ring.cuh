@@ -96,20 +96,34 @@ struct ChunkWalk {
     }
 };
 
-// Producer: issue every chunk of the block, SBYTES at most each, into the ring.
-template <int STAGES, int SV>
-__device__ __forceinline__ void produce(const void* base, const RowLayout& lay, int es,
-                                        int64_t vpr, int64_t start, int64_t end, uint4* ring,
-                                        uint64_t* full, uint64_t* empty) {
+// Producer: issue every chunk of the block, SBYTES at most each, into the ring.  With
+// PEEL the units are elements and each row segment contributes only its 16-byte aligned
+// interior (see peel); otherwise units are whole vectors.
+template <typename T, bool PEEL, int STAGES, int SV>
+__device__ __forceinline__ void produce(const void* base, const RowLayout& lay, int64_t vpr,
+                                        int64_t start, int64_t end, uint4* ring, uint64_t* full,
+                                        uint64_t* empty) {
     ChunkWalk w;
     w.begin(start, end, vpr);
     uint32_t k = 0;
     bool ok = true;
     while (ok && w.pos < w.end) {
-        const uint4* src = reinterpret_cast<const uint4*>(reinterpret_cast<const char*>(base) +
-                                                          lay.offset(w.r) * es);
-        for (int64_t jj = w.j0; jj < w.j1; jj += SV) {
-            const uint32_t n = (uint32_t)min((int64_t)SV, w.j1 - jj);
+        const T* rowp = reinterpret_cast<const T*>(base) + lay.offset(w.r);
+        const uint4* src;
+        int64_t c0, c1;  // the segment's vectors, relative to src
+        if constexpr (PEEL) {
+            int64_t a0, a1;
+            peel(rowp, w.j0, w.j1, a0, a1);
+            src = reinterpret_cast<const uint4*>(rowp + a0);
+            c0 = 0;
+            c1 = (a1 - a0) / DT<T>::kEPV;
+        } else {
+            src = reinterpret_cast<const uint4*>(rowp);
+            c0 = w.j0;
+            c1 = w.j1;
+        }
+        for (int64_t jj = c0; jj < c1; jj += SV) {
+            const uint32_t n = (uint32_t)min((int64_t)SV, c1 - jj);
             const uint32_t s = k % STAGES, use = k / STAGES;
             if (use > 0 && !wait(&empty[s], (use - 1) & 1)) {
                 ok = false;
@@ -154,8 +168,8 @@ __global__ void __launch_bounds__((NCW + 1) * 32, K1_RING_FWD_MINB) k1_fwd_ring_
     const int64_t start = piece_start(b, p.total, G), end = piece_start(b + 1, p.total, G);
     if (warp == NCW) {
         if (lane == 0)
-            ring::produce<STAGES, SV>(p.logits, p.lay, (int)sizeof(T), p.vpr, start, end, ring_buf,
-                                      full, empty);
+            ring::produce<T, false, STAGES, SV>(p.logits, p.lay, p.vpr, start, end, ring_buf,
+                                                full, empty);
         return;
     }
     const int tid = threadIdx.x;
@@ -236,7 +250,11 @@ __global__ void __launch_bounds__((NCW + 1) * 32, K1_RING_FWD_MINB) k1_fwd_ring_
     }
 }
 
-template <typename T, int NCW, int STAGES, int SBYTES, bool SCALED = false>
+// PEEL: rows that are not whole vectors (units are elements); the logits and gradient rows
+// must share their 16-byte misalignment (checked by the launcher).  Each row segment's
+// aligned interior goes through the ring, its head and tail elements are handled by the
+// consumer threads directly.
+template <typename T, int NCW, int STAGES, int SBYTES, bool SCALED = false, bool PEEL = false>
 __global__ void __launch_bounds__((NCW + 1) * 32, K1_RING_MINB) k1_bwd_ring_kernel(BwdParams p) {
     using D = DT<T>;
     constexpr int NC = NCW * 32;
@@ -262,8 +280,8 @@ __global__ void __launch_bounds__((NCW + 1) * 32, K1_RING_MINB) k1_bwd_ring_kern
     const int64_t start = b * p.total / G, end = (b + 1) * p.total / G;
     if (warp == NCW) {
         if (lane == 0)
-            ring::produce<STAGES, SV>(p.logits, p.lay, (int)sizeof(T), p.vpr, start, end, ring_buf,
-                                      full, empty);
+            ring::produce<T, PEEL, STAGES, SV>(p.logits, p.lay, p.vpr, start, end, ring_buf,
+                                               full, empty);
         return;
     }
     const int tid = threadIdx.x;
@@ -274,7 +292,7 @@ __global__ void __launch_bounds__((NCW + 1) * 32, K1_RING_MINB) k1_bwd_ring_kern
     while (w.pos < w.end) {
         const int64_t r = w.r;
         const T* xr = reinterpret_cast<const T*>(p.logits) + p.lay.offset(r);
-        uint4* dv = reinterpret_cast<uint4*>(reinterpret_cast<T*>(p.dlogits) + p.dlay.offset(r));
+        T* dr = reinterpret_cast<T*>(p.dlogits) + p.dlay.offset(r);
         BwdRow q;
         q.lse = p.lse[r];
         q.ent = p.entropy[r];
@@ -287,8 +305,29 @@ __global__ void __launch_bounds__((NCW + 1) * 32, K1_RING_MINB) k1_bwd_ring_kern
             const int64_t tl = tg - p.col_offset;
             q.tl = (tg >= 0 && tl >= 0 && tl < p.vocab) ? tl : -1;
         }
-        for (int64_t jj = w.j0; jj < w.j1; jj += SV) {
-            const int64_t n = min((int64_t)SV, w.j1 - jj);
+        // the segment's vectors [c0, c1) relative to the vector base dv (the producer's
+        // chunks); tl_rel = target column relative to dv's first element
+        uint4* dv;
+        int64_t c0, c1, tl_rel;
+        if constexpr (PEEL) {
+            int64_t a0, a1;
+            peel(xr, w.j0, w.j1, a0, a1);
+            dv = reinterpret_cast<uint4*>(dr + a0);
+            c0 = 0;
+            c1 = (a1 - a0) / EPV;
+            tl_rel = q.tl - a0;
+            const int64_t nh = a0 - w.j0, ne = nh + (w.j1 - a1);  // at most 2 (EPV - 1)
+            if (tid < ne)
+                bwd_element<T, SCALED>(xr, dr, tid < nh ? w.j0 + tid : a1 + (tid - nh), q,
+                                       p.scale);
+        } else {
+            dv = reinterpret_cast<uint4*>(dr);
+            c0 = w.j0;
+            c1 = w.j1;
+            tl_rel = q.tl;
+        }
+        for (int64_t jj = c0; jj < c1; jj += SV) {
+            const int64_t n = min((int64_t)SV, c1 - jj);
             const uint32_t s = k % STAGES, use = k / STAGES;
             if (ok) ok = ring::wait(&full[s], use & 1);
             const uint4* stage = ring_buf + (size_t)s * SV;
@@ -299,7 +338,7 @@ __global__ void __launch_bounds__((NCW + 1) * 32, K1_RING_MINB) k1_bwd_ring_kern
                     if (i < n) {
                         const int64_t jv = jj + i;
                         uint4 o = bwd_vector<T, SCALED>(stage[i], q, p.scale);
-                        const uint64_t kk = (uint64_t)(q.tl - jv * EPV);
+                        const uint64_t kk = (uint64_t)(tl_rel - jv * EPV);
                         if (kk < (uint64_t)EPV)
                             o = vec_set<T>(o, (int)kk, bwd_target_out<T>(xr, q, p.scale));
                         stg_stream(dv + jv, o);

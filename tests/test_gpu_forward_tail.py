@@ -146,3 +146,22 @@ def test_peeled_rows_forward_and_backward(rows, vocab, dtype):
     d2 = xg.clone()
     _C.fused_logprob_entropy_v1_backward(d2, tg, l, h, *(a.cuda() for a in g), d2)
     torch.testing.assert_close(d2, d, rtol=0, atol=0)
+
+
+def test_peeled_backward_gradient_layout_with_other_alignment():
+    """A gradient view whose rows are misaligned differently from the logits rows (a
+    slice of a wider buffer) takes the single-element path; ring, register and element
+    paths compute the same bits."""
+    from _gpu import grads_like
+    from kernel_opt import _C
+    N, V = 3000, 50257
+    x = seeded_logits((N, V), torch.bfloat16, 3.0, seed=77).cuda()
+    t = seeded_targets((N,), V, seed=78).cuda()
+    lp, h, l = kernel_opt.fused_logprob_entropy_forward(x, t)
+    g = [a.cuda() for a in grads_like((N,), seed=79)]
+    d_same = torch.empty_like(x)                       # congruent: peeled ring
+    _C.fused_logprob_entropy_v1_backward(x, t, l, h, *g, d_same)
+    wide = torch.empty((N, V + 3), dtype=x.dtype, device="cuda")
+    d_other = wide[:, 1:V + 1]                         # rows shifted by 2 bytes and 6 per row
+    _C.fused_logprob_entropy_v1_backward(x, t, l, h, *g, d_other)
+    torch.testing.assert_close(d_other, d_same, rtol=0, atol=0)
