@@ -16,7 +16,7 @@
 #include <type_traits>
 #include <utility>
 
-#include "k1_ring.cuh"
+#include "k1_fwd_sm.cuh"
 
 namespace {
 
@@ -133,6 +133,27 @@ constexpr int kMaxOwnersPerSm = 32;  // static pieces + dynamic chunks; sizes th
 #ifndef K1_FWD_ROWS_FORCE_GT
 #define K1_FWD_ROWS_FORCE_GT 0  // measurement builds only: always use this group size
 #endif
+// Forward, one block per SM (k1_fwd_sm_kernel, vector path): at least one row per SM,
+// rows of at least K1_FWD_SM_MIN_CHUNKS chunks (32 x 8 vectors), at most
+// K1_FWD_SM_MAX_CHUNKS_PER_SM chunks per SM in all.  Beyond that the row groups' whole
+// rows cost less than the grabs' merges.  Measured on B200 (forward, bf16, us, row groups
+// or split rows -> one block per SM): 148 x 152064 23.6 -> 19.5, 1024 x 152064 68.6 ->
+// 62.5, 512 x 65536 29.7 -> 21.5, 4096 x 131072 179.2 -> 173.1, 16384 x 65536 353 -> 327;
+// 16384 x 256000 1256 -> 1320 and 8192 x 32000 105.5 -> 107.5 stay on row groups.
+// 0 disables.
+#ifndef K1_FWD_SM
+#define K1_FWD_SM 1
+#endif
+#ifndef K1_FWD_SM_WARPS
+#define K1_FWD_SM_WARPS 16
+#endif
+#ifndef K1_FWD_SM_MIN_CHUNKS
+#define K1_FWD_SM_MIN_CHUNKS 24
+#endif
+#ifndef K1_FWD_SM_MAX_CHUNKS_PER_SM
+#define K1_FWD_SM_MAX_CHUNKS_PER_SM 8192
+#endif
+constexpr int kSmWarps = K1_FWD_SM_WARPS;
 constexpr int64_t kMinUnitsPerBlockVec = (int64_t)kThreads * kUnroll;
 constexpr int64_t kMinUnitsPerBlockScalar = (int64_t)kThreads * 64;
 
@@ -342,6 +363,20 @@ int launch_forward(const char* fn, const void* logits, const Rows& L, int64_t co
             rc = grid_for(kern, dev, p.total, kMinUnitsPerBlockVec, &grid, threads, smem);
             if (rc) return rc;
             launch(kern, grid, threads, smem, stream, p);
+            return check_launch(fn);
+        }
+    }
+    if (K1_FWD_SM && vec) {
+        const int64_t cpr = (p.vpr + 32 * kUnroll - 1) / (32 * kUnroll);
+        if (cpr >= K1_FWD_SM_MIN_CHUNKS && L.n_rows >= sms && p.vpr < (int64_t)1 << 30 &&
+            L.n_rows * cpr <= (int64_t)K1_FWD_SM_MAX_CHUNKS_PER_SM * sms &&
+            L.n_rows <= (int64_t)sms << 20) {
+            auto kern = k1::k1_fwd_sm_kernel<T, kSmWarps, kUnroll, SHARD, SCALED>;
+            const size_t smem = sizeof(k1::SmFwdSmem);
+            int occ = 0;
+            rc = blocks_per_sm(kern, dev, kSmWarps * 32, smem, &occ);
+            if (rc) return rc;
+            launch(kern, std::min<int64_t>(sms, L.n_rows), kSmWarps * 32, smem, stream, p);
             return check_launch(fn);
         }
     }

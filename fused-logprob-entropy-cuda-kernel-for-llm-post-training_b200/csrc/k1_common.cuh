@@ -228,7 +228,10 @@ struct FwdState {
         const bool moved = !(dl == 0.f);
         const float s = moved ? ex2(dl * kLog2e) : 1.f;
         const float2 z = add2(zs, at_max());
-        t = mul2(fma2(splat(dl), z, t), splat(s));
+        // t' = (t + dl z) s, evaluated as (dl s) z + t s: dl s stays within [-1/e, 0] for
+        // any dl, whereas dl z overflows to -inf (and times s = 0 gives NaN) when the
+        // first maximum was a clamped -inf (dl ~ -3.4e38) and several logits sat at it.
+        t = fma2(splat(dl * s), z, mul2(t, splat(s)));
         if (moved) {
             zs = mul2(z, splat(s));
             ms = splat(0.f);

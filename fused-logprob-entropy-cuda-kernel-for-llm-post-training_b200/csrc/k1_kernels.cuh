@@ -283,14 +283,14 @@ __device__ __forceinline__ void fwd_remainder(const uint4* vp, int64_t j, int64_
 // while the current chunk is reduced (two register buffers used alternately): warps that
 // start in lock-step (every warp of the grid issues its first loads together) would
 // otherwise alternate between waiting for memory and computing instead of overlapping.
-template <typename T, bool SCALED, int THREADS, int U>
+template <typename T, bool SCALED, int THREADS, int U, bool PF = (K1_FWD_PREFETCH != 0)>
 __device__ __forceinline__ void fwd_stream_vec(const T* rowp, int64_t j0, int64_t j1,
                                                FwdState& st, int tid, bool clamp, float s) {
     const uint4* vp = reinterpret_cast<const uint4*>(rowp);
     constexpr int64_t kSpan = (int64_t)(U - 1) * THREADS;
     constexpr int64_t kStep = (int64_t)U * THREADS;
     int64_t j = j0 + tid;
-    if constexpr (K1_FWD_PREFETCH) {
+    if constexpr (PF) {
         if (j + kSpan < j1) {
             uint4 a[U], b[U];
             load_fwd<T, SCALED, U, THREADS>(a, vp, j, s);

@@ -165,3 +165,32 @@ def test_peeled_backward_gradient_layout_with_other_alignment():
     d_other = wide[:, 1:V + 1]                         # rows shifted by 2 bytes and 6 per row
     _C.fused_logprob_entropy_v1_backward(x, t, l, h, *g, d_other)
     torch.testing.assert_close(d_other, d_same, rtol=0, atol=0)
+
+
+# A row whose first logits are all -inf: in the clamped re-stream they sit at the lowest
+# finite value as the running maximum of a lane until a finite logit arrives; the
+# rescale then must give exactly 0 for their t terms (not NaN from an overflowing
+# (lowest - m) * count product).
+CLAMPED_PREFIX = [
+    (20000, 4096, torch.bfloat16),    # one-warp row groups
+    (2000, 2048, torch.float16),      # whole-block groups
+    (600, 8192, torch.bfloat16),      # block kernel
+    (300, 32001, torch.bfloat16),     # block kernel, peeled rows
+    (12000, 50257, torch.bfloat16),   # row groups, peeled rows
+    (1024, 152064, torch.bfloat16),   # one block per SM
+    (3000, 4096, torch.float32),
+]
+
+
+@pytest.mark.parametrize("rows,vocab,dtype", CLAMPED_PREFIX)
+def test_rows_with_a_long_minus_inf_prefix(rows, vocab, dtype):
+    x = seeded_logits((rows, vocab), torch.float32, 3.0, seed=rows + 3)
+    t = seeded_targets((rows,), vocab, seed=rows + 4)
+    for i, keep in enumerate((96, 3, 1000, 1, vocab // 2, 2100)):
+        x[i, : vocab - keep] = float("-inf")
+        t[i] = vocab - 1
+    x = x.to(dtype)
+    outs = kernel_opt.fused_logprob_entropy_forward(x.cuda(), t.cuda())
+    idx = torch.cat([torch.arange(0, 8), torch.arange(rows - 8, rows)])
+    check_forward_outputs(tuple(o[idx.cuda()] for o in outs), x[idx], t[idx],
+                          f"-inf prefix {rows}x{vocab} {dtype}")
