@@ -153,7 +153,21 @@ constexpr int kMaxOwnersPerSm = 32;  // static pieces + dynamic chunks; sizes th
 #ifndef K1_FWD_SM_MAX_CHUNKS_PER_SM
 #define K1_FWD_SM_MAX_CHUNKS_PER_SM 8192
 #endif
-constexpr int kSmWarps = K1_FWD_SM_WARPS;
+// The scaled forward (temperature folded in) does more arithmetic per logit: 24 warps
+// without the prefetch buffer beat 16 with it (config 2 scaled 73.7 -> 69.7 us).  Warp
+// count and prefetch do not change a grab's arithmetic, so the scaled forward keeps the
+// same bits as the unscaled one on logits divided beforehand; for that, both select the
+// kernel by the same rule.
+#ifndef K1_FWD_SM_WARPS_SCALED
+#define K1_FWD_SM_WARPS_SCALED 24
+#endif
+#ifndef K1_SM_PREFETCH_SCALED
+#define K1_SM_PREFETCH_SCALED 0
+#endif
+template <bool SCALED>
+constexpr int kSmWarps = SCALED ? K1_FWD_SM_WARPS_SCALED : K1_FWD_SM_WARPS;
+template <bool SCALED>
+constexpr bool kSmPrefetch = SCALED ? (K1_SM_PREFETCH_SCALED != 0) : (K1_SM_PREFETCH != 0);
 constexpr int64_t kMinUnitsPerBlockVec = (int64_t)kThreads * kUnroll;
 constexpr int64_t kMinUnitsPerBlockScalar = (int64_t)kThreads * 64;
 
@@ -371,12 +385,13 @@ int launch_forward(const char* fn, const void* logits, const Rows& L, int64_t co
         if (cpr >= K1_FWD_SM_MIN_CHUNKS && L.n_rows >= sms && p.vpr < (int64_t)1 << 30 &&
             L.n_rows * cpr <= (int64_t)K1_FWD_SM_MAX_CHUNKS_PER_SM * sms &&
             L.n_rows <= (int64_t)sms << 20) {
-            auto kern = k1::k1_fwd_sm_kernel<T, kSmWarps, kUnroll, SHARD, SCALED>;
+            constexpr int nw = kSmWarps<SCALED>;
+            auto kern = k1::k1_fwd_sm_kernel<T, nw, kUnroll, SHARD, SCALED, kSmPrefetch<SCALED>>;
             const size_t smem = sizeof(k1::SmFwdSmem);
             int occ = 0;
-            rc = blocks_per_sm(kern, dev, kSmWarps * 32, smem, &occ);
+            rc = blocks_per_sm(kern, dev, nw * 32, smem, &occ);
             if (rc) return rc;
-            launch(kern, std::min<int64_t>(sms, L.n_rows), kSmWarps * 32, smem, stream, p);
+            launch(kern, std::min<int64_t>(sms, L.n_rows), nw * 32, smem, stream, p);
             return check_launch(fn);
         }
     }

@@ -170,7 +170,7 @@ __device__ __forceinline__ int64_t sm_row_offset(const RowLayout& lay, int64_t r
 
 // One block of NW warps per SM (launch with gridDim.x <= n_rows, rows of fewer than 2^31
 // vectors and sizeof(SmFwdSmem) bytes of dynamic shared memory); vector path only.
-template <typename T, int NW, int U, bool SHARD, bool SCALED>
+template <typename T, int NW, int U, bool SHARD, bool SCALED, bool PF>
 __global__ void __launch_bounds__(NW * 32, 1) k1_fwd_sm_kernel(FwdParams p) {
     extern __shared__ __align__(16) unsigned char k1_sm_raw[];
     SmFwdSmem& sm = *reinterpret_cast<SmFwdSmem*>(k1_sm_raw);
@@ -204,7 +204,7 @@ __global__ void __launch_bounds__(NW * 32, 1) k1_fwd_sm_kernel(FwdParams p) {
         const int a = g * gv, e = min(vpr, a + gv);
         FwdState st;
         st.init();
-        fwd_stream_vec<T, SCALED, 32, U, K1_SM_PREFETCH>(rowp, a, e, st, lane, false, p.scale);
+        fwd_stream_vec<T, SCALED, 32, U, PF>(rowp, a, e, st, lane, false, p.scale);
         if (st.saw_neg_inf()) {
             st.init();
             fwd_stream_vec<T, SCALED, 32, U, false>(rowp, a, e, st, lane, true, p.scale);

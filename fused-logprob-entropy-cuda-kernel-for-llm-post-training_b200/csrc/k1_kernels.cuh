@@ -231,6 +231,12 @@ __device__ __forceinline__ void load_vectors(uint4 (&v)[U], const uint4* vp, int
     for (int u = 0; u < U; ++u) v[u] = ldg_stream(vp + j + (int64_t)u * THREADS);
 }
 
+template <typename T, int U>
+__device__ __forceinline__ void scale_all(uint4 (&v)[U], float s) {
+#pragma unroll
+    for (int u = 0; u < U; ++u) v[u] = scale_vec<T>(v[u], s);
+}
+
 // Forward chunk load; SCALED applies the logit scale to the loaded vectors.
 template <typename T, bool SCALED, int U, int THREADS>
 __device__ __forceinline__ void load_fwd(uint4 (&v)[U], const uint4* vp, int64_t j, float s) {
@@ -291,17 +297,21 @@ __device__ __forceinline__ void fwd_stream_vec(const T* rowp, int64_t j0, int64_
     constexpr int64_t kStep = (int64_t)U * THREADS;
     int64_t j = j0 + tid;
     if constexpr (PF) {
+        // raw loads go out a chunk ahead; the scale is applied when a chunk is consumed
+        // (applying it at load time would wait for the loads right away)
         if (j + kSpan < j1) {
             uint4 a[U], b[U];
-            load_fwd<T, SCALED, U, THREADS>(a, vp, j, s);
+            load_vectors<U, THREADS>(a, vp, j);
             while (true) {
                 bool more = j + kStep + kSpan < j1;
-                if (more) load_fwd<T, SCALED, U, THREADS>(b, vp, j + kStep, s);
+                if (more) load_vectors<U, THREADS>(b, vp, j + kStep);
+                if constexpr (SCALED) scale_all<T, U>(a, s);
                 fwd_chunk<T, U>(a, st, clamp);
                 j += kStep;
                 if (!more) break;
                 more = j + kStep + kSpan < j1;
-                if (more) load_fwd<T, SCALED, U, THREADS>(a, vp, j + kStep, s);
+                if (more) load_vectors<U, THREADS>(a, vp, j + kStep);
+                if constexpr (SCALED) scale_all<T, U>(b, s);
                 fwd_chunk<T, U>(b, st, clamp);
                 j += kStep;
                 if (!more) break;

@@ -102,3 +102,18 @@ def test_sm_shard_partials():
     np.testing.assert_allclose(got["m"], want["m"], rtol=0, atol=0)
     np.testing.assert_allclose(got["z"], want["z"], rtol=1e-5)
     np.testing.assert_allclose(got["x_t"], want["x_t"], rtol=0, atol=0)
+
+
+def test_sm_scaled_equals_divided_at_config2():
+    """The scaled forward runs with more warps and no prefetch buffer; a grab's arithmetic
+    is the same, so it keeps the bits of the unscaled forward on pre-divided logits."""
+    from kernel_opt import _C, grpo
+    N, V, T = 1024, 152064, 0.85
+    x = seeded_logits((N, V), torch.bfloat16, 3.0, seed=41).cuda()
+    t = seeded_targets((N,), V, seed=42).cuda()
+    a = [torch.empty(N, device="cuda") for _ in range(3)]
+    b = [torch.empty(N, device="cuda") for _ in range(3)]
+    _C.fused_logprob_entropy_scaled(x, t, *a, grpo.temperature_scale(T))
+    _C.fused_logprob_entropy_v1(x.clone().div_(T), t, *b)
+    for u, v in zip(a, b):
+        torch.testing.assert_close(u, v, rtol=0, atol=0)
