@@ -5,14 +5,17 @@ Workload (the metric's single-GPU headline): bf16 logits
 [B=8, S=128, V=152064] ~ N(0, 3^2), targets sampled per row from softmax(logits),
 upstream gradients g_logp = -1/N, g_entropy = -0.01/N.  A step is one forward and one
 backward over that batch through the public API (kernel_opt.fused_logprob_entropy +
-torch.autograd.grad), inputs resident in HBM.  With --gpus N under torchrun every rank
-processes its own batch (row-sharded, weak scaling, no collective in the data path).
+torch.autograd.grad), inputs resident in HBM.  `value` times that step captured once as a
+CUDA graph and replayed (the same two kernel launches per step without the per-step
+Python launch overhead); the eager steps are timed too (`eager`) and give the forward /
+backward split.  With --gpus N under torchrun every rank processes its own batch
+(row-sharded, weak scaling, no collective in the data path).
 
 Metric: algorithmic bytes per step / time, fwd = N V s + 20 N, bwd = 2 N V s + 28 N
 (s = 2 for bf16), reported in GB/s together with rows/s.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                  [--config c2|c3|c4-bf16|c4-fp16|c4-fp32] [--no-cpu-baseline]
+                  [--config c2|c3|c4-bf16|c4-fp16|c4-fp32] [--no-cpu-baseline] [--eager]
 
 --impl reference times the reference's CPU path (TRL-1.4 selective_log_softmax +
 entropy_from_logits + autograd, restated in oracle/trl_eager.py since TRL is not
@@ -498,9 +501,20 @@ def ours_arm(args, cfg, rank, local_rank, world):
     barrier()
 
     # ---- device-resident timing (value) --------------------------------------------
+    # Eager steps (one Python call per op; their per-kernel events give the forward /
+    # backward split), then the same step captured once as a CUDA graph and replayed K
+    # times: identical launches and work, without the per-step host launch overhead, which
+    # otherwise dominates once several processes share one host.
     K = args.steps
     ev = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(K)]
     start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+
+    def max_over_ranks(ms):
+        t = torch.tensor([ms], device=device, dtype=torch.float64)
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
     with ClockSampler(device) as clocks:
         barrier()
         start.record(stream)
@@ -514,13 +528,32 @@ def ours_arm(args, cfg, rank, local_rank, world):
             del d, lp, h, _l, x
         stop.record(stream)
         barrier()
-    total_ms = start.elapsed_time(stop)
+        eager_ms = max_over_ranks(start.elapsed_time(stop))
+        graph, graph_ms = None, None
+        if not args.eager:
+            # capture after the eager steps: capturing empties torch's allocator cache
+            side = torch.cuda.Stream(device)
+            side.wait_stream(stream)
+            with torch.cuda.stream(side):
+                for _ in range(3):
+                    step()
+            stream.wait_stream(side)
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph, stream=side):
+                step()
+            for _ in range(max(3, args.warmup)):
+                graph.replay()
+            barrier()
+            start.record(stream)
+            for _ in range(K):
+                graph.replay()
+            stop.record(stream)
+            barrier()
+            graph_ms = max_over_ranks(start.elapsed_time(stop))
     fwd_ms = [e[0].elapsed_time(e[1]) for e in ev]
     bwd_ms = [e[1].elapsed_time(e[2]) for e in ev]
-    t = torch.tensor([total_ms], device=device, dtype=torch.float64)
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    max_ms = float(t.item())
+    max_ms = graph_ms if graph_ms is not None else eager_ms
+    del graph
 
     # ---- end to end through the public API with host buffers (e2e) ----------------
     pin = dict(pin_memory=True)
@@ -595,8 +628,14 @@ def ours_arm(args, cfg, rank, local_rank, world):
         "config": {"workload": cfg["workload"], "global_batch": cfg["B"] * world,
                    "seq_len": cfg["S"], "vocab": V, "rows_per_gpu": N,
                    "parallelism": f"row-sharded x{world} (no collective)",
+                   "step": ("one CUDA-graph replay of the captured fwd + bwd step"
+                            if graph_ms is not None else "eager fwd + bwd calls"),
                    "l2": (f"inputs larger than L2: {logits.numel() * esize / 2**20:.0f} MiB "
                           f"logits read and written per step vs {L2_BYTES // 2**20} MiB L2")},
+        "eager": {"value": round(step_bytes * K * world / (eager_ms / 1e3) / 1e9, 2),
+                  "ms_per_step": round(eager_ms / K, 4),
+                  "note": "kernel_opt.fused_logprob_entropy + torch.autograd.grad called "
+                          "from Python every step"},
         "roofline": {"bound": "hbm", "kernel": "k1_bwd_ring_kernel", "achieved": round(achieved, 1),
                      "peak": peak, "unit": "GB/s", "frac": round(achieved / peak, 4),
                      "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs, copy)",
@@ -1009,6 +1048,8 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--config", choices=sorted(CONFIGS), default="c2")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--eager", action="store_true",
+                    help="time eager steps only (no CUDA-graph replay of the step)")
     ap.add_argument("--mode", choices=["rows", "vocab", "grpo", "lmhead"], default="rows",
                     help="rows: row-sharded (default); vocab: vocab-parallel (config c5); "
                          "grpo: the GRPO loss block on config c3, fused vs unfused; "
