@@ -1112,8 +1112,7 @@ __global__ void k1_vocab_combine_kernel(const k1_partial* g, int n_shards, int64
     acc.m = -INFINITY;
     acc.pad = 0.f;
     double xt = 0.0;
-    for (int k = 0; k < n_shards; ++k) {
-        const k1_partial q = g[(int64_t)k * n_rows + r];
+    auto fold = [&](const k1_partial& q) {
         RowPartial pk;
         pk.z = q.z;
         pk.t = q.t;
@@ -1121,6 +1120,18 @@ __global__ void k1_vocab_combine_kernel(const k1_partial* g, int n_shards, int64
         pk.pad = 0.f;
         acc = merge_partials(acc, pk);
         if (q.has_target) xt = (double)q.x_t;
+    };
+    // up to kBatch shards' partials are loaded before the first merge (one memory round
+    // trip instead of one per shard); the merge order is the shard order either way
+    constexpr int kBatch = 8;
+    for (int k0 = 0; k0 < n_shards; k0 += kBatch) {
+        k1_partial q[kBatch];
+#pragma unroll
+        for (int i = 0; i < kBatch; ++i)
+            if (k0 + i < n_shards) q[i] = g[(int64_t)(k0 + i) * n_rows + r];
+#pragma unroll
+        for (int i = 0; i < kBatch; ++i)
+            if (k0 + i < n_shards) fold(q[i]);
     }
     finalize_row(acc, xt, logprob + r, entropy + r, lse + r);
 }
