@@ -81,10 +81,11 @@ const char* k1_last_error(void);
 int k1_abi_version(void);
 
 /*
- * Diagnostic: the kernels that stream through a shared-memory ring of bulk copies bound
- * every wait on the ring's barriers; a wait that runs out sets a per-device word instead
- * of hanging.  This reads and clears that word for the current device (*out = 0: no wait
- * ran out).  Synchronises with the device.  No counterpart in the reference.
+ * Diagnostic: every wait inside a kernel is bounded; a wait that runs out sets a bit of a
+ * per-device word instead of hanging (bit 0: a barrier of the bulk-copy ring; bit 2: a
+ * row slot of the one-block-per-SM forward).  This reads and clears that word for the
+ * current device (*out = 0: no wait ran out).  Synchronises with the device.  No
+ * counterpart in the reference.
  */
 int k1_ring_status(unsigned* out);
 
