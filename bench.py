@@ -474,7 +474,12 @@ def ours_arm(args, cfg, rank, local_rank, world):
 
     device = torch.device("cuda", local_rank)
     torch.cuda.set_device(device)
+    bound = None
     if world > 1:
+        # one process per GPU: run on the host cores next to this GPU, so the pinned
+        # buffers of the e2e leg sit on its NUMA node (no cross-socket copies)
+        from kernel_opt import host as k1_host
+        bound = k1_host.bind_to_device_cpus(device)
         dist.init_process_group("nccl", rank=rank, world_size=world, device_id=device,
                                 timeout=datetime.timedelta(seconds=300))
     V, dt = cfg["V"], cfg["dtype"]
@@ -646,7 +651,9 @@ def ours_arm(args, cfg, rank, local_rank, world):
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h_outputs,
                 "ms_per_step": round(e2e_ms / K2, 3), "steps": K2,
                 "note": "logits, targets and upstream grads from pinned host memory; "
-                        "logprob/entropy/lse read back; the logits gradient stays on the GPU"},
+                        "logprob/entropy/lse read back; the logits gradient stays on the GPU",
+                "host_cpus_rank0": (f"bound to the {len(bound)} cores NVML reports next to "
+                                    "the GPU" if bound else "process affinity unchanged")},
         "e2e_gradient_to_host": {
             "value": round(step_bytes * K2 * world / (e2e_host_grad_ms / 1e3) / 1e9, 3),
             "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h_with_grad,

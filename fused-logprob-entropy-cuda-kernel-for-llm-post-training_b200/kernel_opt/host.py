@@ -19,6 +19,8 @@ can run right after its forward.  Rows are independent, so chunking changes no r
 """
 from __future__ import annotations
 
+import os
+
 import torch
 
 from kernel_opt import _C
@@ -32,6 +34,48 @@ def _streams(dev: torch.device):
     if dev not in _STREAMS:
         _STREAMS[dev] = tuple(torch.cuda.Stream(dev) for _ in range(3))
     return _STREAMS[dev]
+
+
+def gpu_local_cpus(device, nvml=None) -> set[int] | None:
+    """The host CPUs that NVML reports as closest to `device` (the cores of the NUMA node
+    its PCIe link hangs off), or None when NVML is missing or cannot tell.  `nvml` is the
+    NVML module to use (default: pynvml)."""
+    if nvml is None:
+        try:
+            import pynvml as nvml
+        except ImportError:
+            return None
+    props = torch.cuda.get_device_properties(torch.device(device))
+    bus = f"{props.pci_domain_id:08x}:{props.pci_bus_id:02x}:{props.pci_device_id:02x}.0"
+    n_cpu = os.cpu_count() or 1
+    try:
+        nvml.nvmlInit()
+        try:
+            h = nvml.nvmlDeviceGetHandleByPciBusId(bus)
+            masks = nvml.nvmlDeviceGetCpuAffinity(h, (n_cpu + 63) // 64)
+        finally:
+            nvml.nvmlShutdown()
+    except Exception:
+        return None
+    cpus = {64 * i + b for i, m in enumerate(masks) for b in range(64) if (int(m) >> b) & 1}
+    return cpus or None
+
+
+def bind_to_device_cpus(device, nvml=None) -> set[int] | None:
+    """Restrict this process to the host CPUs closest to `device` (see gpu_local_cpus),
+    within its current affinity, so that host memory it allocates from then on -- pinned
+    staging buffers in particular -- is placed on that NUMA node and host<->device copies
+    do not cross the socket interconnect.  Meant for one process per GPU; call it before
+    allocating host buffers.  Returns the CPUs bound to, or None (nothing changed) when
+    the GPU's CPUs are unknown or none of them is allowed."""
+    cpus = gpu_local_cpus(device, nvml)
+    if not cpus:
+        return None
+    allowed = cpus & os.sched_getaffinity(0)
+    if not allowed:
+        return None
+    os.sched_setaffinity(0, allowed)
+    return allowed
 
 
 def chunk_schedule(n_rows: int, chunk_rows: int, ramp: int = 3) -> list[tuple[int, int]]:

@@ -161,3 +161,43 @@ def test_host_chunk_schedule_covers_rows_once_and_ramps():
     s = chunk_schedule(1024, 110)
     sizes = [b - a for a, b in s]
     assert sizes[:3] == [13, 27, 55] and sizes[-3:] == [55, 27, 13]
+
+
+class _FakeNvml:
+    """NVML stand-in: one GPU whose CPU affinity mask is `masks`."""
+
+    def __init__(self, masks, fail=False):
+        self.masks, self.fail, self.bus = masks, fail, None
+
+    def nvmlInit(self):
+        if self.fail:
+            raise RuntimeError("no NVML")
+
+    def nvmlShutdown(self):
+        pass
+
+    def nvmlDeviceGetHandleByPciBusId(self, bus):
+        self.bus = bus
+        return object()
+
+    def nvmlDeviceGetCpuAffinity(self, handle, n_words):
+        return self.masks[:n_words]
+
+
+def test_gpu_local_cpus_and_binding(monkeypatch):
+    import types
+    from kernel_opt import host
+    props = types.SimpleNamespace(pci_domain_id=0, pci_bus_id=0x18, pci_device_id=0)
+    monkeypatch.setattr(host.torch.cuda, "get_device_properties", lambda d: props)
+    fake = _FakeNvml([0b1011])
+    assert host.gpu_local_cpus("cuda:0", fake) == {0, 1, 3}
+    assert fake.bus == "00000000:18:00.0"
+    assert host.gpu_local_cpus("cuda:0", _FakeNvml([0], fail=True)) is None
+    assert host.gpu_local_cpus("cuda:0", _FakeNvml([0])) is None
+    calls = []
+    monkeypatch.setattr(host.os, "sched_getaffinity", lambda pid: {1, 2, 3})
+    monkeypatch.setattr(host.os, "sched_setaffinity", lambda pid, cpus: calls.append(set(cpus)))
+    assert host.bind_to_device_cpus("cuda:0", _FakeNvml([0b1011])) == {1, 3}
+    assert calls == [{1, 3}]
+    assert host.bind_to_device_cpus("cuda:0", _FakeNvml([0b10000])) is None  # none allowed
+    assert calls == [{1, 3}]
