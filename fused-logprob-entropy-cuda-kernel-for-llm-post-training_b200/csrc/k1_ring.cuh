@@ -22,6 +22,16 @@
 #ifndef K1_RING_FWD_MINB
 #define K1_RING_FWD_MINB 1
 #endif
+// The backward's producer issues its first STAGES bulk copies before waiting for the
+// previous kernel of the stream (programmatic dependent launch), so they overlap that
+// kernel's tail.  It only reads the logits there.  No kernel of this library writes the
+// logits of a later backward: the forward and the vocab-parallel combine only read them,
+// and an in-place backward writes a gradient that no later launch takes as its logits.
+// Kernels of other libraries are not launched as programmatic primaries, so a backward
+// after one of them starts only once it has completed.  0 waits before the first copy.
+#ifndef K1_RING_EARLY
+#define K1_RING_EARLY 1
+#endif
 
 namespace k1 {
 
@@ -99,7 +109,9 @@ struct ChunkWalk {
 // Producer: issue every chunk of the block, SBYTES at most each, into the ring.  With
 // PEEL the units are elements and each row segment contributes only its 16-byte aligned
 // interior (see peel); otherwise units are whole vectors.
-template <typename T, bool PEEL, int STAGES, int SV>
+// EARLY: the first STAGES copies go out before this thread waits for the previous kernel
+// of the stream (pdl_wait); otherwise the caller has waited already.
+template <typename T, bool PEEL, int STAGES, int SV, bool EARLY = false>
 __device__ __forceinline__ void produce(const void* base, const RowLayout& lay, int64_t vpr,
                                         int64_t start, int64_t end, uint4* ring, uint64_t* full,
                                         uint64_t* empty) {
@@ -107,6 +119,7 @@ __device__ __forceinline__ void produce(const void* base, const RowLayout& lay, 
     w.begin(start, end, vpr);
     uint32_t k = 0;
     bool ok = true;
+    bool waited = !EARLY;
     while (ok && w.pos < w.end) {
         const T* rowp = reinterpret_cast<const T*>(base) + lay.offset(w.r);
         const uint4* src;
@@ -125,6 +138,10 @@ __device__ __forceinline__ void produce(const void* base, const RowLayout& lay, 
         for (int64_t jj = c0; jj < c1; jj += SV) {
             const uint32_t n = (uint32_t)min((int64_t)SV, c1 - jj);
             const uint32_t s = k % STAGES, use = k / STAGES;
+            if (!waited && k == (uint32_t)STAGES) {
+                pdl_wait();
+                waited = true;
+            }
             if (use > 0 && !wait(&empty[s], (use - 1) & 1)) {
                 ok = false;
                 break;
@@ -135,6 +152,7 @@ __device__ __forceinline__ void produce(const void* base, const RowLayout& lay, 
         }
         w.next_row(vpr);
     }
+    if (!waited) pdl_wait();
     // drain: every issued copy has landed before this thread returns
     for (uint32_t i = (k > (uint32_t)STAGES ? k - STAGES : 0u); i < k; ++i)
         wait(&full[i % STAGES], (i / STAGES) & 1);
@@ -266,7 +284,7 @@ __global__ void __launch_bounds__((NCW + 1) * 32, K1_RING_MINB) k1_bwd_ring_kern
     __shared__ __align__(8) uint64_t full[STAGES];
     __shared__ __align__(8) uint64_t empty[STAGES];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    pdl_wait();
+    if (!K1_RING_EARLY) pdl_wait();
     pdl_trigger();
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; ++s) {
@@ -280,10 +298,11 @@ __global__ void __launch_bounds__((NCW + 1) * 32, K1_RING_MINB) k1_bwd_ring_kern
     const int64_t start = b * p.total / G, end = (b + 1) * p.total / G;
     if (warp == NCW) {
         if (lane == 0)
-            ring::produce<T, PEEL, STAGES, SV>(p.logits, p.lay, p.vpr, start, end, ring_buf,
-                                               full, empty);
+            ring::produce<T, PEEL, STAGES, SV, K1_RING_EARLY != 0>(p.logits, p.lay, p.vpr, start,
+                                                                  end, ring_buf, full, empty);
         return;
     }
+    if (K1_RING_EARLY) pdl_wait();  // the consumers read the forward's outputs
     const int tid = threadIdx.x;
     ring::ChunkWalk w;
     w.begin(start, end, p.vpr);
