@@ -7,19 +7,34 @@ upstream gradients g_logp = -1/N, g_entropy = -0.01/N.  A step is one forward an
 backward over that batch through the public API (kernel_opt.fused_logprob_entropy +
 torch.autograd.grad), inputs resident in HBM.  `value` times that step captured once as a
 CUDA graph and replayed (the same two kernel launches per step without the per-step
-Python launch overhead); the eager steps are timed too (`eager`) and give the forward /
-backward split.  With --gpus N under torchrun every rank processes its own batch
-(row-sharded, weak scaling, no collective in the data path).
+Python launch overhead); the eager steps are timed too (`eager`).  With --gpus N under
+torchrun every rank processes its own batch (row-sharded, weak scaling, no collective in
+the data path).
+
+Also on the line:
+  fwd / bwd, roofline.per_kernel -- each launch of the step timed alone on the device: a
+      CUDA graph of (L2 flush, launch) replayed between CUDA events, minus a flush-only
+      graph;
+  c3, c4_bf16, c4_fp16, c4_fp32 (N = 1) -- the same per-launch figures for config 3 (the
+      strided GRPO window, 16 384 x 151 936: the north-star shape) and config 4 per dtype;
+  vocab_parallel -- config 5 [32768, 256000] over the same N ranks, vocabulary sharded,
+      one NCCL all-gather of partials per forward (strong scaling), the all-gather timed
+      alone, and a 128-row parity check against an fp64 torch recomputation;
+  e2e -- the step from pinned host buffers through kernel_opt.host (host<->device copies
+      inside the timed region);
+  cpu_baseline (N = 1) -- the reference's CPU path on the host cores.
 
 Metric: algorithmic bytes per step / time, fwd = N V s + 20 N, bwd = 2 N V s + 28 N
 (s = 2 for bf16), reported in GB/s together with rows/s.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
                   [--config c2|c3|c4-bf16|c4-fp16|c4-fp32] [--no-cpu-baseline] [--eager]
+                  [--no-extra-configs] [--no-vocab-parallel]
+                  [--mode rows|vocab|grpo|lmhead]
 
 --impl reference times the reference's CPU path (TRL-1.4 selective_log_softmax +
 entropy_from_logits + autograd, restated in oracle/trl_eager.py since TRL is not
-installed) on the host cores, on rank 0 only.
+installed) on the host cores, on rank 0 only, with every host thread the process may use.
 """
 from __future__ import annotations
 
@@ -293,6 +308,9 @@ def dist_env():
 def reference_arm(args, cfg, rank, world):
     if rank != 0:
         return
+    # torchrun sets OMP_NUM_THREADS=1 for every rank; the reference's CPU path gets all
+    # the host threads this process may use, at every N
+    torch.set_num_threads(len(os.sched_getaffinity(0)))
     from oracle import trl_eager
     V, dt = cfg["V"], cfg["dtype"]
     esize = torch.tensor([], dtype=dt).element_size()
@@ -327,13 +345,14 @@ def reference_arm(args, cfg, rank, world):
         "ms_per_step": round(el / args.steps * 1e3, 3), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": DTYPE_NAME[dt], "data": "synthetic",
         "rows_per_s": round(n_rows * args.steps / el, 2),
-        "config": {"workload": cfg["workload"], "global_batch": B, "seq_len": S, "vocab": V,
-                   "rows_per_step": n_rows, "parallelism": "cpu host threads"},
+        "config": arm_config(cfg, world, esize),
         "cpu_baseline": {"value": round(value, 4), "unit": UNIT, "cores": torch.get_num_threads(),
                          "kind": "port",
-                         "sample": f"{b_use}/{B} batch elements ({n_rows} rows x {V}) per step; "
-                                   "TRL-1.4 selective_log_softmax + entropy_from_logits + "
-                                   "autograd, restated in oracle/trl_eager.py"},
+                         "sample": f"{b_use}/{B} batch elements ({n_rows} rows x {V}) per step "
+                                   "on rank 0's host threads; TRL-1.4 selective_log_softmax + "
+                                   "entropy_from_logits + autograd, restated in "
+                                   "oracle/trl_eager.py",
+                         "host_cores": host_cores()},
         "e2e": {"value": round(value, 4), "unit": UNIT, "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
@@ -467,6 +486,239 @@ def time_reference_k1_gpu(cfg, iters=20):
                     "(oracle/build_ref.py), same shape, CUDA events, median of %d" % iters}
 
 
+def arm_config(cfg, world, esize):
+    """The `config` object both arms print (identical keys and values for one workload and
+    GPU count, so the two lines can be matched)."""
+    n_rows = cfg["B"] * cfg["S"]
+    return {"workload": cfg["workload"], "global_batch": cfg["B"] * world, "seq_len": cfg["S"],
+            "vocab": cfg["V"], "rows_per_gpu": n_rows,
+            "parallelism": f"row-sharded x{world} (no collective)",
+            "l2": (f"inputs larger than L2: {n_rows * cfg['V'] * esize / 2**20:.0f} MiB of "
+                   f"logits read and written per step vs {L2_BYTES // 2**20} MiB L2")}
+
+
+# ---------------------------------------------------------------------------------------
+# Device-true kernel timing: one launch per CUDA graph, L2 flushed before it
+# ---------------------------------------------------------------------------------------
+class GraphTimer:
+    """Times single launches on the device.  A launch is captured in a CUDA graph behind a
+    write of a buffer twice the size of L2 (so it starts cold, as it would after any other
+    large kernel), the graph is replayed K times between two CUDA events on the launching
+    stream, and the same measurement of a graph holding the flush alone is subtracted."""
+
+    def __init__(self, device, stream):
+        self.device, self.stream = device, stream
+        self.flush = torch.empty(2 * L2_BYTES, dtype=torch.uint8, device=device)
+        self.graphs = []
+        self.g_flush = self.capture(lambda: None)
+
+    def capture(self, fn):
+        side = torch.cuda.Stream(self.device)
+        side.wait_stream(self.stream)
+        with torch.cuda.stream(side):
+            for _ in range(3):
+                self.flush.zero_()
+                fn()
+        self.stream.wait_stream(side)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=side):
+            self.flush.zero_()
+            fn()
+        torch.cuda.synchronize(self.device)
+        self.graphs.append(g)
+        return g
+
+    def replay_ms(self, g, K):
+        for _ in range(3):
+            g.replay()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(self.stream)
+        for _ in range(K):
+            g.replay()
+        b.record(self.stream)
+        b.synchronize()
+        return a.elapsed_time(b) / K
+
+    def kernel_ms(self, fn, K, reps=3):
+        """Median over `reps` of (flush + launch) - (flush), per launch, in ms."""
+        g = self.capture(fn)
+        vals = sorted(self.replay_ms(g, K) - self.replay_ms(self.g_flush, K) for _ in range(reps))
+        return vals[len(vals) // 2]
+
+    def close(self):
+        self.graphs.clear()
+        del self.flush
+
+
+def kernel_legs(timer, logits, targets, g_lp, g_h, K, peak):
+    """The workload's forward and backward launches (the ones the autograd step makes),
+    each timed alone by `timer`, with bytes, GB/s and fraction of the measured peak."""
+    from kernel_opt import _C
+    N, V = targets.numel(), logits.shape[-1]
+    esize = logits.element_size()
+    fwd_bytes, bwd_bytes = algorithmic_bytes(N, V, esize)
+    tg = targets.contiguous()
+    gl, gh = g_lp.contiguous(), g_h.contiguous()
+    lp, h, l = (torch.empty(targets.shape, device=logits.device) for _ in range(3))
+    d = torch.empty(logits.shape, dtype=logits.dtype, device=logits.device)
+
+    def fwd():
+        _C.fused_logprob_entropy_v1(logits, tg, lp, h, l)
+
+    def bwd():
+        _C.fused_logprob_entropy_v1_backward(logits, tg, l, h, gl, gh, None, d)
+
+    fwd()
+    f_ms = timer.kernel_ms(fwd, K)
+    b_ms = timer.kernel_ms(bwd, K)
+
+    def entry(ms, nbytes, what):
+        gbs = nbytes / (ms / 1e3) / 1e9
+        return {"kernel": what, "ms": round(ms, 5), "algorithmic_bytes": nbytes,
+                "gbs": round(gbs, 1), "frac": round(gbs / peak, 4),
+                "rows_per_s": round(N / (ms / 1e3), 1)}
+
+    return {"fwd": entry(f_ms, fwd_bytes, "forward launch (kernel chosen by shape)"),
+            "bwd": entry(b_ms, bwd_bytes, "backward launch (k1_bwd_ring_kernel on the vector path)")}
+
+
+def extra_config_legs(device, stream, timer, peak, K, names=("c3", "c4-bf16", "c4-fp16", "c4-fp32")):
+    """Forward / backward launches of the other BASELINE shapes on this GPU (N = 1 only):
+    config 3 (the GRPO window logits[:, :-1] of [16, 1025, 151936], the north-star
+    16 384 x 151 936 shape) and config 4 in each dtype."""
+    out = {}
+    for name in names:
+        cfg = CONFIGS[name]
+        logits, targets, g_lp, g_h = make_workload(cfg, device, seed=777)
+        legs = kernel_legs(timer, logits, targets, g_lp, g_h, K, peak)
+        N = targets.numel()
+        esize = logits.element_size()
+        fb, bb = algorithmic_bytes(N, cfg["V"], esize)
+        step_ms = legs["fwd"]["ms"] + legs["bwd"]["ms"]
+        out[name.replace("-", "_")] = {
+            "workload": cfg["workload"], "rows": N, "vocab": cfg["V"], "dtype": DTYPE_NAME[cfg["dtype"]],
+            "strided_window": bool(cfg["window"]), **legs,
+            "fwd_plus_bwd": {"ms": round(step_ms, 5),
+                             "gbs": round((fb + bb) / (step_ms / 1e3) / 1e9, 1),
+                             "frac": round((fb + bb) / (step_ms / 1e3) / 1e9 / peak, 4)}}
+        del logits, targets, g_lp, g_h
+        torch.cuda.empty_cache()
+    return out
+
+
+def vocab_parallel_leg(args, rank, world, device, stream, barrier, max_over_ranks, peak):
+    """Config 5, vocab-parallel (tensor-parallel LM head layout), strong scaling: rank k holds
+    columns vocab_shard(256000, world, k) of all 32 768 rows; forward = shard partials, ONE
+    NCCL all-gather of [N, 4] float64 partials, merge; backward local.  Also times the
+    all-gather alone and checks 128 rows against an fp64 torch recomputation."""
+    import torch.distributed as dist
+
+    from kernel_opt import parallel
+    cfg = CONFIGS["c5"]
+    N, V, dt = cfg["B"] * cfg["S"], cfg["V"], cfg["dtype"]
+    esize = torch.tensor([], dtype=dt).element_size()
+    cols = parallel.vocab_shard(V, world, rank)
+    Vr = cols.stop - cols.start
+    gen = torch.Generator(device=device).manual_seed(7000 + rank)
+    xs = torch.empty((N, Vr), dtype=dt, device=device)
+    for a in range(0, N, 1024):
+        b = min(N, a + 1024)
+        xs[a:b] = (torch.randn((b - a, Vr), generator=gen, device=device) * cfg["scale"]).to(dt)
+    targets = torch.randint(0, V, (N,), generator=torch.Generator(device=device).manual_seed(99),
+                            device=device)
+    g_lp = torch.full((N,), -1.0 / N, device=device)
+    g_h = torch.full((N,), -0.01 / N, device=device)
+
+    def step():
+        x = xs.detach().requires_grad_(True)
+        lp, h, l = parallel.vocab_parallel_fused_logprob_entropy(x, targets, cols.start)
+        (d,) = torch.autograd.grad((lp, h), x, (g_lp, g_h))
+        return lp, h, l, d
+
+    for _ in range(3):
+        step()
+    barrier()
+    K = max(1, min(args.steps, 50))
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    a.record(stream)
+    for _ in range(K):
+        step()
+    b.record(stream)
+    barrier()
+    ms = max_over_ranks(a.elapsed_time(b)) / K
+
+    # the collective alone: the same all-gather of [N, 4] float64 partials, K times
+    ag_ms = 0.0
+    if world > 1:
+        part = torch.zeros((N, parallel.PARTIAL_WORDS), dtype=torch.float64, device=device)
+        for _ in range(3):
+            parallel.exchange_partials(part)
+        barrier()
+        a.record(stream)
+        for _ in range(K):
+            parallel.exchange_partials(part)
+        b.record(stream)
+        barrier()
+        ag_ms = max_over_ranks(a.elapsed_time(b)) / K
+
+    # parity: 128 rows, the full vocabulary gathered from every shard, against fp64 torch
+    lp, h, l, d = step()
+    idx = torch.linspace(0, N - 1, 128, device=device).round().long()
+    sub = xs[idx].contiguous()
+    if world > 1:
+        parts = [torch.empty_like(sub) for _ in range(world)]
+        dist.all_gather(parts, sub)
+        full = torch.cat(parts, dim=1)
+    else:
+        full = sub
+    barrier()
+    parity = None
+    if rank == 0:
+        x64 = full.double()
+        t = targets[idx]
+        logp_all = torch.log_softmax(x64, dim=-1)
+        p = logp_all.exp()
+        ent0 = -(p * logp_all).sum(-1)
+        lse0 = torch.logsumexp(x64, dim=-1)
+        lp0 = logp_all.gather(1, t[:, None]).squeeze(1)
+        gl, gh = g_lp[idx].double()[:, None], g_h[idx].double()[:, None]
+        d0 = -gl * p - gh * p * (logp_all + ent0[:, None])
+        d0.scatter_add_(1, t[:, None], gl)
+        d0 = d0[:, cols.start:cols.stop]
+        dd = d[idx].double()
+        floor = 1e-7 * float(d0.abs().max())
+        grad_rel = float(((dd - d0).abs() / (d0.abs() + floor)).max())
+        parity = {
+            "rows_checked": 128, "reference": "fp64 torch log_softmax / logsumexp on the "
+                                              "gathered full-vocabulary rows",
+            "lse_max_abs_err": float((l[idx].double() - lse0).abs().max()),
+            "logp_max_abs_err": float((lp[idx].double() - lp0).abs().max()),
+            "entropy_max_rel_err": float(((h[idx].double() - ent0).abs() / ent0.abs()).max()),
+            "grad_max_rel_err_rank0_shard": grad_rel,
+        }
+        parity["within_tolerance"] = bool(parity["lse_max_abs_err"] <= 1e-5
+                                          and parity["logp_max_abs_err"] <= 1e-5
+                                          and parity["entropy_max_rel_err"] <= 1e-4
+                                          and grad_rel <= 1e-2)
+    del xs, d
+    torch.cuda.empty_cache()
+    fwd, bwd = algorithmic_bytes(N, V, esize)
+    gbs = (fwd + bwd) / (ms / 1e3) / 1e9
+    return {"workload": cfg["workload"], "rows": N, "vocab": V, "vocab_per_gpu": Vr,
+            "n_gpus": world, "scaling": "strong", "steps": K,
+            "ms_per_step": round(ms, 4), "gbs_total": round(gbs, 1),
+            "gbs_per_gpu": round(gbs / world, 1), "pct_of_peak_per_gpu": round(100 * gbs / world / peak, 2),
+            "rows_per_s": round(N / (ms / 1e3), 1),
+            "collective": ("NCCL all_gather_into_tensor of [N, 4] float64 partials "
+                           f"({N * 32} bytes per rank), one per forward" if world > 1
+                           else "none (one process holds the whole vocabulary)"),
+            "allgather_ms": round(ag_ms, 4),
+            "allgather_share_of_step": round(ag_ms / ms, 4) if ms > 0 else None,
+            "parity": parity,
+            "step": "eager: vocab_parallel_fused_logprob_entropy + torch.autograd.grad"}
+
+
 def ours_arm(args, cfg, rank, local_rank, world):
     import torch.distributed as dist
 
@@ -489,6 +741,7 @@ def ours_arm(args, cfg, rank, local_rank, world):
     fwd_bytes, bwd_bytes = algorithmic_bytes(N, V, esize)
     step_bytes = fwd_bytes + bwd_bytes
     stream = torch.cuda.current_stream(device)
+    peak, peak_kind = measured_peak_gbs()
 
     def step():
         x = logits.detach().requires_grad_(True)
@@ -501,35 +754,29 @@ def ours_arm(args, cfg, rank, local_rank, world):
             dist.barrier(device_ids=[local_rank])
         torch.cuda.synchronize(device)
 
-    for _ in range(max(3, args.warmup)):
-        step()
-    barrier()
-
-    # ---- device-resident timing (value) --------------------------------------------
-    # Eager steps (one Python call per op; their per-kernel events give the forward /
-    # backward split), then the same step captured once as a CUDA graph and replayed K
-    # times: identical launches and work, without the per-step host launch overhead, which
-    # otherwise dominates once several processes share one host.
-    K = args.steps
-    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(K)]
-    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-
     def max_over_ranks(ms):
         t = torch.tensor([ms], device=device, dtype=torch.float64)
         if world > 1:
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
 
+    for _ in range(max(3, args.warmup)):
+        step()
+    barrier()
+
+    # ---- device-resident timing (value) --------------------------------------------
+    # Eager steps (one Python call per op), then the same step captured once as a CUDA
+    # graph and replayed K times: identical launches and work, without the per-step host
+    # launch overhead, which otherwise dominates once several processes share one host.
+    K = args.steps
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(device) as clocks:
         barrier()
         start.record(stream)
         for i in range(K):
             x = logits.detach().requires_grad_(True)
-            ev[i][0].record(stream)
             lp, h, _l = kernel_opt.fused_logprob_entropy(x, targets)
-            ev[i][1].record(stream)
             (d,) = torch.autograd.grad((lp, h), x, (g_lp, g_h))
-            ev[i][2].record(stream)
             del d, lp, h, _l, x
         stop.record(stream)
         barrier()
@@ -555,10 +802,18 @@ def ours_arm(args, cfg, rank, local_rank, world):
             stop.record(stream)
             barrier()
             graph_ms = max_over_ranks(start.elapsed_time(stop))
-    fwd_ms = [e[0].elapsed_time(e[1]) for e in ev]
-    bwd_ms = [e[1].elapsed_time(e[2]) for e in ev]
     max_ms = graph_ms if graph_ms is not None else eager_ms
     del graph
+
+    # ---- each kernel alone, device-true (graph replays, L2 flushed before each) --------
+    timer = GraphTimer(device, stream)
+    legs = kernel_legs(timer, logits, targets, g_lp, g_h, max(10, min(K, 50)), peak)
+    extra = None
+    if world == 1 and not args.no_extra_configs:
+        extra = extra_config_legs(device, stream, timer, peak, max(5, min(K, 20)))
+    timer.close()
+    del timer
+    torch.cuda.empty_cache()
 
     # ---- end to end through the public API with host buffers (e2e) ----------------
     pin = dict(pin_memory=True)
@@ -595,20 +850,26 @@ def ours_arm(args, cfg, rank, local_rank, world):
             e2e_step(d_logits)
         e1.record(stream)
         barrier()
-        ms = torch.tensor([e0.elapsed_time(e1)], device=device, dtype=torch.float64)
-        if world > 1:
-            dist.all_reduce(ms, op=dist.ReduceOp.MAX)
-        return float(ms.item())
+        return max_over_ranks(e0.elapsed_time(e1))
 
     # the step's result (per-row log-prob / entropy / lse) comes back to the host; the
     # logits gradient stays in HBM, where a training step's next backward op reads it
     e2e_ms = time_e2e(d_dev)
     # offload variant: the gradient also goes back to host memory
     e2e_host_grad_ms = time_e2e(d_h)
+    del logits_h, d_h, d_dev
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu = time_cpu_baseline(logits, targets, g_lp, g_h, esize)
+
+    # ---- config 5, vocab-parallel over the same ranks (one NCCL all-gather) -----------
+    vocab = None
+    if not args.no_vocab_parallel:
+        del logits
+        torch.cuda.empty_cache()
+        vocab = vocab_parallel_leg(args, rank, world, device, stream, barrier, max_over_ranks,
+                                   peak)
 
     if world > 1:
         dist.barrier(device_ids=[local_rank])
@@ -616,11 +877,8 @@ def ours_arm(args, cfg, rank, local_rank, world):
     if rank != 0:
         return
 
-    peak, peak_kind = measured_peak_gbs()
     value = step_bytes * K * world / (max_ms / 1e3) / 1e9
-    bwd_avg = statistics.mean(bwd_ms)
-    fwd_avg = statistics.mean(fwd_ms)
-    achieved = bwd_bytes / (bwd_avg / 1e3) / 1e9
+    fwd_ms, bwd_ms = legs["fwd"]["ms"], legs["bwd"]["ms"]
     cfg_name = args.config
     out = {
         "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world, "steps": K,
@@ -628,24 +886,33 @@ def ours_arm(args, cfg, rank, local_rank, world):
         "scaling": "weak", "vs_baseline": None, "dtype": DTYPE_NAME[dt], "data": "synthetic",
         "rows_per_s": round(N * K * world / (max_ms / 1e3), 1),
         "pct_of_peak": round(100 * value / world / peak, 2),
-        "fwd": {"ms": round(fwd_avg, 5), "gbs": round(fwd_bytes / (fwd_avg / 1e3) / 1e9, 1)},
-        "bwd": {"ms": round(bwd_avg, 5), "gbs": round(achieved, 1)},
-        "config": {"workload": cfg["workload"], "global_batch": cfg["B"] * world,
-                   "seq_len": cfg["S"], "vocab": V, "rows_per_gpu": N,
-                   "parallelism": f"row-sharded x{world} (no collective)",
-                   "step": ("one CUDA-graph replay of the captured fwd + bwd step"
-                            if graph_ms is not None else "eager fwd + bwd calls"),
-                   "l2": (f"inputs larger than L2: {logits.numel() * esize / 2**20:.0f} MiB "
-                          f"logits read and written per step vs {L2_BYTES // 2**20} MiB L2")},
+        "config": arm_config(cfg, world, esize),
+        "step": ("one CUDA-graph replay of the captured fwd + bwd step (kernel_opt."
+                 "fused_logprob_entropy + torch.autograd.grad), inputs resident in HBM"
+                 if graph_ms is not None else "eager fwd + bwd calls"),
+        "fwd": legs["fwd"], "bwd": legs["bwd"],
+        "kernel_timing": ("each launch alone in a CUDA graph behind a write of "
+                          f"{2 * L2_BYTES // 2**20} MiB (L2 flush), replayed between CUDA "
+                          "events; the flush-only graph's time subtracted; median of 3"),
         "eager": {"value": round(step_bytes * K * world / (eager_ms / 1e3) / 1e9, 2),
                   "ms_per_step": round(eager_ms / K, 4),
                   "note": "kernel_opt.fused_logprob_entropy + torch.autograd.grad called "
                           "from Python every step"},
-        "roofline": {"bound": "hbm", "kernel": "k1_bwd_ring_kernel", "achieved": round(achieved, 1),
-                     "peak": peak, "unit": "GB/s", "frac": round(achieved / peak, 4),
+        "roofline": {"bound": "hbm", "kernel": "k1_bwd_ring_kernel",
+                     "achieved": legs["bwd"]["gbs"], "peak": peak, "unit": "GB/s",
+                     "frac": legs["bwd"]["frac"],
                      "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs, copy)",
                      "algorithmic_bytes_per_launch": bwd_bytes,
-                     "traffic": committed_traffic(cfg_name)},
+                     "launch_ms": round(bwd_ms, 5),
+                     "traffic": committed_traffic(cfg_name),
+                     "per_kernel": [
+                         {"kernel": "forward", "achieved": legs["fwd"]["gbs"],
+                          "frac": legs["fwd"]["frac"], "launch_ms": round(fwd_ms, 5),
+                          "algorithmic_bytes_per_launch": fwd_bytes},
+                         {"kernel": "backward (k1_bwd_ring_kernel)", "achieved": legs["bwd"]["gbs"],
+                          "frac": legs["bwd"]["frac"], "launch_ms": round(bwd_ms, 5),
+                          "algorithmic_bytes_per_launch": bwd_bytes}],
+                     "kernels_sum_over_step": round((fwd_ms + bwd_ms) / (max_ms / K), 4)},
         "gpu_launches": 2 * K,
         "e2e": {"value": round(step_bytes * K2 * world / (e2e_ms / 1e3) / 1e9, 3), "unit": UNIT,
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h_outputs,
@@ -660,6 +927,10 @@ def ours_arm(args, cfg, rank, local_rank, world):
             "ms_per_step": round(e2e_host_grad_ms / K2, 3), "steps": K2},
         "clocks": clocks.summary(),
     }
+    if extra is not None:
+        out.update(extra)
+    if vocab is not None:
+        out["vocab_parallel"] = vocab
     if cpu is not None:
         out["cpu_baseline"] = cpu
     print(json.dumps(out), flush=True)
@@ -1055,6 +1326,10 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--config", choices=sorted(CONFIGS), default="c2")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-extra-configs", action="store_true",
+                    help="skip the config 3 / config 4 kernel legs of the N = 1 line")
+    ap.add_argument("--no-vocab-parallel", action="store_true",
+                    help="skip the config 5 vocab-parallel sub-record")
     ap.add_argument("--eager", action="store_true",
                     help="time eager steps only (no CUDA-graph replay of the step)")
     ap.add_argument("--mode", choices=["rows", "vocab", "grpo", "lmhead"], default="rows",

@@ -4,6 +4,9 @@ Produces
   kernel_opt/lib/libk1_b200.so   C ABI (include/k1_logprob.h), CUDA kernels, no torch
   kernel_opt/_C<ext>.so          torch extension mirroring the reference's `_C`
                                  binding, linked against libk1_b200.so
+  kernel_opt/lib/libk1_b200_waittest.so
+                                 the C ABI with short wait limits and test knobs, for
+                                 the wait-timeout GPU test only
 
 Run `python build.py` (or `build()` from Python).  Outputs are rebuilt only when a
 source is newer than the output, unless force=True.
@@ -65,6 +68,23 @@ def build_capi(force: bool = False, verbose_ptxas: bool = False) -> str:
     return CAPI_LIB
 
 
+# The wait-timeout test library: the same C ABI built with short wait limits and the
+# K1_WAIT_TEST knobs (k1_test_set_knobs), so a GPU test can make a kernel's bounded waits
+# run out and check that the kernel returns, reports the status bit and writes NaN.  The
+# product never loads it.
+WAIT_TEST_LIB = os.path.join(LIBDIR, "libk1_b200_waittest.so")
+WAIT_TEST_FLAGS = ["-DK1_WAIT_TEST", "-DK1_RING_MAX_TRIES=16", "-DK1_SM_MAX_POLLS=4096"]
+
+
+def build_wait_test_lib(force: bool = False) -> str:
+    srcs = [os.path.join(CSRC, s) for s in CAPI_SOURCES] + [os.path.join(INCLUDE, "k1_logprob.h")]
+    if force or _stale(WAIT_TEST_LIB, srcs):
+        os.makedirs(LIBDIR, exist_ok=True)
+        _run([_nvcc(), *NVCC_FLAGS, *WAIT_TEST_FLAGS, "-I", INCLUDE,
+              os.path.join(CSRC, "k1_capi.cu"), "-o", WAIT_TEST_LIB])
+    return WAIT_TEST_LIB
+
+
 def binding_path() -> str:
     suffix = sysconfig.get_config_var("EXT_SUFFIX") or ".so"
     return os.path.join(PKG, "_C" + suffix)
@@ -99,6 +119,7 @@ def build_binding(force: bool = False) -> str:
 def build(force: bool = False) -> None:
     build_capi(force=force)
     build_binding(force=force)
+    build_wait_test_lib(force=force)
 
 
 if __name__ == "__main__":

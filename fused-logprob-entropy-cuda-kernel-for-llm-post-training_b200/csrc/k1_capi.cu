@@ -862,4 +862,18 @@ int k1_vocab_shard_backward(const void* logits, int dtype, int64_t n_rows, int64
                          d_outer_stride, stream);
 }
 
+#ifdef K1_WAIT_TEST
+// Only in the wait-timeout test library (built with -DK1_WAIT_TEST and short wait limits;
+// not part of libk1_b200.so): sets the knobs that make one block's bounded waits run out
+// on the current device.  withhold: the backward ring's block 0 issues no bulk copy from
+// that chunk on; skip_grab: the one-block-per-SM forward's block 0 drops that grab.  -1
+// turns a knob off.
+int k1_test_set_knobs(long long withhold, long long skip_grab) {
+    cudaError_t e = cudaMemcpyToSymbol(k1::k1_test_withhold, &withhold, sizeof withhold);
+    if (e == cudaSuccess) e = cudaMemcpyToSymbol(k1::k1_test_skip_grab, &skip_grab, sizeof skip_grab);
+    if (e != cudaSuccess) return fail(K1_ERR_CUDA, "k1_test_set_knobs: %s", cudaGetErrorString(e));
+    return K1_OK;
+}
+#endif
+
 }  // extern "C"

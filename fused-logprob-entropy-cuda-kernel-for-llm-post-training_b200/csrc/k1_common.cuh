@@ -98,6 +98,7 @@ struct DT<__nv_bfloat16> {
     static constexpr uint32_t kLowest2 = 0xFF7FFF7Fu;  // lowest finite bf16, both halves
     static constexpr float kLowest = -3.38953138925153547590470800371487866880e38f;
     static constexpr uint32_t kPadWord = kLowest2;  // vector padding: contributes e = 0
+    static constexpr uint32_t kNaNWord = 0x7FC07FC0u;  // quiet NaN, both halves
     __device__ static __forceinline__ uint32_t clamp2(uint32_t w) {
         uint32_t r;
         asm("max.NaN.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(w), "r"(kLowest2));
@@ -160,6 +161,7 @@ struct DT<__half> {
     static constexpr uint32_t kLowest2 = 0xFBFFFBFFu;  // -65504, both halves
     static constexpr float kLowest = -65504.0f;
     static constexpr uint32_t kPadWord = kLowest2;
+    static constexpr uint32_t kNaNWord = 0x7E007E00u;  // quiet NaN, both halves
     __device__ static __forceinline__ uint32_t clamp2(uint32_t w) {
         uint32_t r;
         asm("max.NaN.f16x2 %0, %1, %2;" : "=r"(r) : "r"(w), "r"(kLowest2));
@@ -194,6 +196,7 @@ struct DT<float> {
     static constexpr int kEPV = 4;
     static constexpr float kLowest = kClampF32;
     static constexpr uint32_t kPadWord = 0xFE967699u;  // bits of -1.0e38f
+    static constexpr uint32_t kNaNWord = 0x7FC00000u;  // quiet NaN
     __device__ static __forceinline__ float load1(const float* p) { return *p; }
     __device__ static __forceinline__ void store1(float* p, float v) { *p = v; }
     __device__ static __forceinline__ float clamp1(float x) { return fmax_nan(x, kClampF32); }

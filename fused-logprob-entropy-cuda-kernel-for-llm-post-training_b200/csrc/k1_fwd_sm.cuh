@@ -25,7 +25,8 @@
 // row j - R has been merged (its grabs were handed out at least R - 1 rows earlier, so
 // this wait is normally already over).  Every wait depends only on warps of the same
 // block holding grabs of earlier rows, so it always ends; it is still bounded (polls with
-// a suspend hint) and sets bit 2 of k1_ring_error instead of hanging.
+// a suspend hint) and sets bit 2 of k1_ring_error instead of hanging, and the two rows it
+// leaves unfinished get NaN outputs.
 #pragma once
 
 #include "k1_ring.cuh"
@@ -57,7 +58,19 @@ struct SmFwdSmem {
     int next;            // next grab of the block's sequence
 };
 
-constexpr int kSmMaxPolls = 1 << 22;  // x ~1 us suspend hint per poll
+// Polls of a row-slot wait before it gives up (each poll sleeps about 64 ns or more).
+// The wait-timeout test library is built with a small value.
+#ifndef K1_SM_MAX_POLLS
+#define K1_SM_MAX_POLLS (1 << 22)
+#endif
+constexpr int kSmMaxPolls = K1_SM_MAX_POLLS;
+
+#ifdef K1_WAIT_TEST
+// Test-only knob (compiled into the wait-timeout test library only): block 0 drops its
+// grab number k1_test_skip_grab instead of parking it, so that row never completes and
+// the row that next needs its slot waits until the wait runs out.  -1: off.
+__device__ long long k1_test_skip_grab = -1;
+#endif
 
 // Grab geometry of a row of `cpr` chunks: chunks per grab and grabs per row.
 __device__ __forceinline__ void sm_grabs(int64_t cpr, int& gc, int& gpr) {
@@ -157,6 +170,36 @@ __device__ __forceinline__ void sm_merge(const FwdParams& p, SmFwdSmem& sm, int 
     }
 }
 
+// A slot wait ran out (k1_ring_error bit 2 is set): the warp could not park its grab of
+// block-local row j, and the row still holding the slot can no longer complete either.
+// Both rows' outputs become NaN, so the failure shows without the host reading the
+// error word.
+template <bool SHARD>
+__device__ __forceinline__ void sm_fail(const FwdParams& p, const SmFwdSmem& sm, int j, int lane) {
+    if (lane != 0) return;
+    const float nan = __int_as_float(0x7fc00000);
+    const int jo = *(volatile const int*)&sm.slot_row[j % SmFwdSmem::R];
+    const int64_t rows[2] = {blockIdx.x + (int64_t)j * gridDim.x,
+                             (jo >= 0 && jo < j) ? blockIdx.x + (int64_t)jo * gridDim.x : -1};
+    for (int i = 0; i < 2; ++i) {
+        const int64_t r = rows[i];
+        if (r < 0 || r >= p.n_rows) continue;
+        if constexpr (SHARD) {
+            k1_partial o;
+            o.z = o.t = (double)nan;
+            o.m = nan;
+            o.x_t = nan;
+            o.has_target = 0;
+            o.reserved = 0;
+            p.partials[r] = o;
+        } else {
+            p.logprob[r] = nan;
+            p.entropy[r] = nan;
+            p.lse[r] = nan;
+        }
+    }
+}
+
 // Element offset of row r; 32-bit division when the operands fit (the common case).
 __device__ __forceinline__ int64_t sm_row_offset(const RowLayout& lay, int64_t r) {
     if (lay.inner_rows == 1) return r * lay.outer_stride;
@@ -217,7 +260,15 @@ __global__ void __launch_bounds__(NW * 32, 1) k1_fwd_sm_kernel(FwdParams p) {
             cap = true;
             if (lane == 0) xt = target_logit<T>(rowp + tt, p.scale);
         }
-        if (sm_store<T>(sm, j, g, st, cap, xt, lane) && sm_count(sm, j, gpr, lane))
+#ifdef K1_WAIT_TEST
+        if (b == 0 && (long long)k == k1_test_skip_grab) {
+            k = __shfl_sync(0xffffffffu, kn, 0);
+            continue;
+        }
+#endif
+        if (!sm_store<T>(sm, j, g, st, cap, xt, lane))
+            sm_fail<SHARD>(p, sm, j, lane);
+        else if (sm_count(sm, j, gpr, lane))
             sm_merge<SHARD>(p, sm, j, gpr, r, has, lane);
         k = __shfl_sync(0xffffffffu, kn, 0);
     }

@@ -22,24 +22,37 @@
 #ifndef K1_RING_FWD_MINB
 #define K1_RING_FWD_MINB 1
 #endif
-// The backward's producer issues its first STAGES bulk copies before waiting for the
+// 1: the backward's producer issues its first STAGES bulk copies before waiting for the
 // previous kernel of the stream (programmatic dependent launch), so they overlap that
-// kernel's tail.  It only reads the logits there.  No kernel of this library writes the
-// logits of a later backward: the forward and the vocab-parallel combine only read them,
-// and an in-place backward writes a gradient that no later launch takes as its logits.
-// Kernels of other libraries are not launched as programmatic primaries, so a backward
-// after one of them starts only once it has completed.  0 waits before the first copy.
+// kernel's tail.  That read of the logits is only correct when the previous kernel does
+// not write them, which the library cannot know: a GEMM that produced the logits right
+// before the backward (an LM head) may trigger its dependents before its last stores,
+// and only griddepcontrol.wait makes a primary's writes visible.  The gain was under 1 %
+// of a step, so every build waits before its first copy (0).
 #ifndef K1_RING_EARLY
-#define K1_RING_EARLY 1
+#define K1_RING_EARLY 0
+#endif
+
+// Polls of a bounded mbarrier wait before it gives up (each poll suspends for at most
+// kSuspendHintNs).  The wait-timeout test library is built with a small value.
+#ifndef K1_RING_MAX_TRIES
+#define K1_RING_MAX_TRIES 4096
 #endif
 
 namespace k1 {
 
 __device__ unsigned k1_ring_error;
 
+#ifdef K1_WAIT_TEST
+// Test-only knob (compiled into the wait-timeout test library only): block 0's producer
+// issues no copy from its chunk number k1_test_withhold on, so the consumers' waits for
+// that chunk run out.  -1: off.
+__device__ long long k1_test_withhold = -1;
+#endif
+
 namespace ring {
 
-constexpr int kMaxTries = 4096;           // x up to 1 ms suspend hint per poll
+constexpr int kMaxTries = K1_RING_MAX_TRIES;  // x up to 1 ms suspend hint per poll
 constexpr uint32_t kSuspendHintNs = 1000000;
 
 __device__ __forceinline__ uint32_t saddr(const void* p) {
@@ -146,6 +159,12 @@ __device__ __forceinline__ void produce(const void* base, const RowLayout& lay, 
                 ok = false;
                 break;
             }
+#ifdef K1_WAIT_TEST
+            if (blockIdx.x == 0 && (long long)k == k1_test_withhold) {
+                ok = false;
+                break;
+            }
+#endif
             arrive_expect(&full[s], n * 16u);
             bulk_g2s(ring + (size_t)s * SV, src + jj, n * 16u, &full[s]);
             ++k;
@@ -362,6 +381,16 @@ __global__ void __launch_bounds__((NCW + 1) * 32, K1_RING_MINB) k1_bwd_ring_kern
                             o = vec_set<T>(o, (int)kk, bwd_target_out<T>(xr, q, p.scale));
                         stg_stream(dv + jv, o);
                     }
+                }
+            } else {
+                // a wait ran out (k1_ring_error is set): this thread's share of every
+                // remaining chunk becomes NaN, so the failure shows in the gradient
+                // without the host reading the error word
+                const uint32_t nw = DT<T>::kNaNWord;
+#pragma unroll
+                for (int u = 0; u < VPT; ++u) {
+                    const int64_t i = tid + u * NC;
+                    if (i < n) stg_stream(dv + jj + i, make_uint4(nw, nw, nw, nw));
                 }
             }
             __syncwarp();

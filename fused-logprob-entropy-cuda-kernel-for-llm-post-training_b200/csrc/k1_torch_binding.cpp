@@ -16,6 +16,8 @@
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
 
+#include <atomic>
+#include <cstdlib>
 #include <map>
 #include <mutex>
 #include <utility>
@@ -81,6 +83,33 @@ int dtype_code(const at::Tensor& x) {
 
 void check_rc(int rc) {
     TORCH_CHECK(rc == K1_OK, k1_last_error());
+}
+
+// Opt-in check of the kernels' bounded waits (K1_CHECK_WAITS=1 in the environment, or
+// _C.set_check_waits(True)).  A wait inside a kernel that runs out sets a device word and
+// leaves NaN in the outputs it could not finish; with the check on, every compute call
+// then synchronises its stream, reads and clears that word and raises.  Off by default
+// (it synchronises); skipped while the current stream is being captured into a graph.
+std::atomic<bool>& check_waits_flag() {
+    static std::atomic<bool> flag{[] {
+        const char* e = std::getenv("K1_CHECK_WAITS");
+        return e != nullptr && e[0] != '\0' && e[0] != '0';
+    }()};
+    return flag;
+}
+
+void check_launch(int rc) {
+    check_rc(rc);
+    if (!check_waits_flag().load(std::memory_order_relaxed)) return;
+    cudaStream_t s = at::cuda::getCurrentCUDAStream().stream();
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    if (cudaStreamIsCapturing(s, &cs) != cudaSuccess || cs != cudaStreamCaptureStatusNone) return;
+    const cudaError_t e = cudaStreamSynchronize(s);
+    TORCH_CHECK(e == cudaSuccess, "k1: ", cudaGetErrorString(e));
+    unsigned v = 0;
+    check_rc(k1_ring_status(&v));
+    TORCH_CHECK(v == 0, "k1: a bounded wait inside a K1 kernel ran out (status ", v,
+                "); the outputs it could not finish hold NaN");
 }
 
 Rows logits_rows(const at::Tensor& logits) {
@@ -149,7 +178,7 @@ void fused_logprob_entropy_v1(at::Tensor logits, at::Tensor targets, at::Tensor 
     c10::cuda::CUDAGuard guard(logits.device());
     size_t ws_bytes = 0;
     void* ws = forward_workspace(logits, &ws_bytes);
-    check_rc(k1_fused_logprob_entropy_v1(
+    check_launch(k1_fused_logprob_entropy_v1(
         logits.data_ptr(), dt, L.n_rows, L.vocab, L.inner_rows, L.inner_stride, L.outer_stride,
         targets.data_ptr<int64_t>(), logprob.data_ptr<float>(), entropy.data_ptr<float>(),
         lse_out.data_ptr<float>(), ws, ws_bytes, at::cuda::getCurrentCUDAStream().stream()));
@@ -168,7 +197,7 @@ void fused_logprob_entropy_scaled(at::Tensor logits, at::Tensor targets, at::Ten
     c10::cuda::CUDAGuard guard(logits.device());
     size_t ws_bytes = 0;
     void* ws = forward_workspace(logits, &ws_bytes);
-    check_rc(k1_fused_logprob_entropy_scaled(
+    check_launch(k1_fused_logprob_entropy_scaled(
         logits.data_ptr(), dt, L.n_rows, L.vocab, L.inner_rows, L.inner_stride, L.outer_stride,
         (float)scale, targets.data_ptr<int64_t>(), logprob.data_ptr<float>(),
         entropy.data_ptr<float>(), lse_out.data_ptr<float>(), ws, ws_bytes,
@@ -184,7 +213,7 @@ void fused_logprob_entropy_naive(at::Tensor logits, at::Tensor targets, at::Tens
     check_fwd_common(logits, targets, logprob, entropy, lse_out, L.n_rows);
     if (L.n_rows == 0) return;
     c10::cuda::CUDAGuard guard(logits.device());
-    check_rc(k1_fused_logprob_entropy_naive(
+    check_launch(k1_fused_logprob_entropy_naive(
         logits.data_ptr(), dt, L.n_rows, L.vocab, L.inner_rows, L.inner_stride, L.outer_stride,
         targets.data_ptr<int64_t>(), logprob.data_ptr<float>(), entropy.data_ptr<float>(),
         lse_out.data_ptr<float>(), at::cuda::getCurrentCUDAStream().stream()));
@@ -266,7 +295,7 @@ void backward_common(const char* which, at::Tensor logits, at::Tensor targets, i
             targets.data_ptr<int64_t>(), lse.data_ptr<float>(), entropy.data_ptr<float>(), gl, ge,
             gs, d_logits.data_ptr(), D.inner_stride, D.outer_stride, s);
     }
-    check_rc(rc);
+    check_launch(rc);
 }
 
 // _C.fused_logprob_entropy_v1_backward (reference csrc/fused_logprob.cu:284-346)
@@ -305,7 +334,7 @@ void vocab_shard_partials(at::Tensor logits, at::Tensor targets, int64_t vocab_o
     c10::cuda::CUDAGuard guard(logits.device());
     size_t ws_bytes = 0;
     void* ws = forward_workspace(logits, &ws_bytes);
-    check_rc(k1_vocab_shard_partials(logits.data_ptr(), dt, L.n_rows, L.vocab, L.inner_rows,
+    check_launch(k1_vocab_shard_partials(logits.data_ptr(), dt, L.n_rows, L.vocab, L.inner_rows,
                                      L.inner_stride, L.outer_stride, vocab_offset,
                                      targets.data_ptr<int64_t>(),
                                      reinterpret_cast<k1_partial*>(partials.data_ptr()), ws,
@@ -331,7 +360,7 @@ void vocab_combine(at::Tensor gathered, int64_t n_shards, at::Tensor logprob, at
                 "outputs must be contiguous");
     if (n_rows == 0) return;
     c10::cuda::CUDAGuard guard(gathered.device());
-    check_rc(k1_vocab_combine(reinterpret_cast<const k1_partial*>(gathered.data_ptr()),
+    check_launch(k1_vocab_combine(reinterpret_cast<const k1_partial*>(gathered.data_ptr()),
                               (int)n_shards, n_rows, logprob.data_ptr<float>(),
                               entropy.data_ptr<float>(), lse_out.data_ptr<float>(),
                               at::cuda::getCurrentCUDAStream().stream()));
@@ -380,4 +409,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
             return v;
         },
         "Read and clear the bulk-copy ring's timeout word of the current device (0 = ok).");
+    m.def(
+        "set_check_waits", [](bool on) { check_waits_flag().store(on); },
+        "Raise after any K1 call whose kernel's bounded wait ran out (synchronises each call).");
+    m.def(
+        "check_waits", []() { return check_waits_flag().load(); },
+        "Whether K1 calls check the kernels' bounded waits (K1_CHECK_WAITS / set_check_waits).");
 }

@@ -25,6 +25,20 @@ from .ops import (  # noqa: F401
 from .lm_head import fused_linear_logprob_entropy  # noqa: F401
 
 
+def set_check_waits(on: bool = True) -> None:
+    """Debug switch: raise a RuntimeError from any K1 call whose kernel's bounded wait ran
+    out.  Every wait inside the kernels is bounded; one that runs out (it cannot in correct
+    operation) leaves NaN in the outputs it could not finish and sets a device status word.
+    With the switch on, each call synchronises its stream and reads that word.  Also set by
+    K1_CHECK_WAITS=1 in the environment.  No counterpart in the reference."""
+    _C.set_check_waits(bool(on))
+
+
+def check_waits() -> bool:
+    """Whether K1 calls check the kernels' bounded waits (see set_check_waits)."""
+    return bool(_C.check_waits())
+
+
 def __getattr__(name):
     # Lazy import so users without trl can still use the kernels.
     if name == "KernelOptGRPOTrainer":

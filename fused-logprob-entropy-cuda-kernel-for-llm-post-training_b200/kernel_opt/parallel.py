@@ -43,9 +43,13 @@ def vocab_shard(vocab: int, world_size: int, rank: int) -> slice:
 
 
 def exchange_partials(partials: torch.Tensor, group=None) -> torch.Tensor:
-    """Step 2: all-gather [N, 4] float64 partials into [world, N, 4] (rank-major)."""
-    world = dist.get_world_size(group)
+    """Step 2: all-gather [N, 4] float64 partials into [world, N, 4] (rank-major).  Without
+    an initialised process group (one process holding the whole vocabulary) there is
+    nothing to exchange: [1, N, 4]."""
     n = partials.shape[0]
+    if group is None and not (dist.is_available() and dist.is_initialized()):
+        return partials.contiguous().view((1, n) + tuple(partials.shape[1:]))
+    world = dist.get_world_size(group)
     out = torch.empty((world * n,) + tuple(partials.shape[1:]), dtype=partials.dtype,
                       device=partials.device)
     dist.all_gather_into_tensor(out, partials.contiguous(), group=group)

@@ -128,7 +128,10 @@ int k1_fused_logprob_entropy_v1(const void* logits, int dtype, int64_t n_rows, i
  * current; make that first call before any stream capture.  Each call clears the part
  * of the array that must start at zero.  All calls on a device share the array: calls
  * that may overlap on the GPU (different streams, concurrent host threads) race and must
- * be serialised by the caller.  No counterpart in the reference.
+ * be serialised by the caller.  The looked-up address is kept for the life of the
+ * process: after cudaDeviceReset (or any reset of the device's primary context) the array
+ * is reloaded at a new address, so calls after a reset are not supported.
+ * No counterpart in the reference.
  */
 int k1_fused_logprob_entropy_v1_noalloc(const void* logits, int dtype, int64_t n_rows,
                                         int64_t vocab, int64_t inner_rows, int64_t inner_stride,

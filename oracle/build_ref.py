@@ -18,7 +18,17 @@ import sys
 HERE = os.path.dirname(os.path.abspath(__file__))
 OUT = os.path.join(HERE, "_ref")
 NAME = "k1_reference"
-DEFAULT_REF = os.environ.get("K1_REFERENCE_ROOT", "/root/reference")
+
+
+def reference_root() -> str | None:
+    """The reference checkout: $K1_REFERENCE_ROOT, else a directory named `reference` beside
+    this repository; None when neither holds the K1 sources."""
+    env = os.environ.get("K1_REFERENCE_ROOT")
+    cands = [env] if env else [os.path.join(os.path.dirname(os.path.dirname(HERE)), "reference")]
+    for c in cands:
+        if c and os.path.exists(os.path.join(c, "csrc", "fused_logprob.cu")):
+            return c
+    return None
 
 
 def built_path() -> str | None:
@@ -26,7 +36,10 @@ def built_path() -> str | None:
     return hits[0] if hits else None
 
 
-def build(ref_root: str = DEFAULT_REF, force: bool = False) -> str | None:
+def build(ref_root: str | None = None, force: bool = False) -> str | None:
+    ref_root = ref_root or reference_root()
+    if ref_root is None:
+        return built_path()
     srcs = [os.path.join(ref_root, "csrc", "bindings.cpp"),
             os.path.join(ref_root, "csrc", "fused_logprob.cu")]
     if not all(os.path.exists(s) for s in srcs):

@@ -12,6 +12,8 @@ from conftest import PKG_ROOT, REPO
 GOLDEN = os.path.join(REPO, "tests", "golden", "k1_golden.npz")
 HEADER = os.path.join(REPO, "include", "k1_logprob.h")
 CAPI_LIB = os.path.join(PKG_ROOT, "kernel_opt", "lib", "libk1_b200.so")
+# the same C ABI built with short wait limits and the K1_WAIT_TEST knobs (test only)
+WAIT_TEST_LIB = os.path.join(PKG_ROOT, "kernel_opt", "lib", "libk1_b200_waittest.so")
 
 TORCH_DT = {"float32": torch.float32, "float16": torch.float16, "bfloat16": torch.bfloat16}
 

@@ -27,3 +27,20 @@ def pytest_collection_modifyitems(config, items):
     for item in items:
         if "gpu" in item.keywords:
             item.add_marker(skip)
+
+
+@pytest.fixture(autouse=True, scope="module")
+def _kernel_waits_never_ran_out():
+    """After every test module that used the GPU: no bounded wait inside a K1 kernel ran
+    out (the kernels report that in a device word instead of hanging; read and cleared
+    here, so a timeout anywhere fails the suite)."""
+    yield
+    try:
+        import torch
+        if not (torch.cuda.is_available() and torch.cuda.is_initialized()):
+            return
+        from kernel_opt import _C
+    except Exception:  # pragma: no cover
+        return
+    status = _C.ring_status()
+    assert status == 0, f"a bounded wait inside a K1 kernel ran out (status {status})"

@@ -4,7 +4,7 @@ import ctypes
 
 import pytest
 
-from _helpers import CAPI_LIB, header_functions
+from _helpers import CAPI_LIB, WAIT_TEST_LIB, header_functions
 
 K1_OK, K1_ERR_INVALID, K1_ERR_DTYPE, K1_ERR_WS = 0, 1, 2, 3
 
@@ -26,6 +26,16 @@ def test_header_declares_expected_entry_points():
 def test_every_declared_symbol_is_exported(lib):
     missing = [n for n in header_functions() if not hasattr(lib, n)]
     assert not missing, f"declared but not exported: {missing}"
+
+
+def test_wait_test_knobs_only_in_the_test_library(lib):
+    """The wait-timeout knobs are compiled into the test library alone; the product library
+    has no way to make a kernel's wait run out."""
+    assert not hasattr(lib, "k1_test_set_knobs")
+    test_lib = ctypes.CDLL(WAIT_TEST_LIB)
+    assert hasattr(test_lib, "k1_test_set_knobs")
+    missing = [n for n in header_functions() if not hasattr(test_lib, n)]
+    assert not missing
 
 
 def test_abi_version(lib):
