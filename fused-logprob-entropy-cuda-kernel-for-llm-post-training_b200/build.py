@@ -25,7 +25,8 @@ PKG = os.path.join(HERE, "kernel_opt")
 LIBDIR = os.path.join(PKG, "lib")
 INCLUDE = os.path.join(REPO, "include")
 
-CAPI_SOURCES = ["k1_capi.cu", "k1_kernels.cuh", "k1_common.cuh", "k1_ring.cuh", "k1_fwd_sm.cuh"]
+CAPI_SOURCES = ["k1_capi.cu", "k1_kernels.cuh", "k1_common.cuh", "k1_ring.cuh", "k1_fwd_sm.cuh",
+                "k1_lmhead.cuh"]
 CAPI_LIB = os.path.join(LIBDIR, "libk1_b200.so")
 BINDING_SOURCE = "k1_torch_binding.cpp"
 

@@ -7,6 +7,9 @@
 // layer, k1_torch_binding.cpp), and every kernel gets a grid of
 // (SM count) x (resident blocks per SM) blocks that split the flattened work evenly.
 #include <algorithm>
+#include <vector>
+#include <tuple>
+#include <cmath>
 #include <atomic>
 #include <cstdarg>
 #include <cstdio>
@@ -17,6 +20,7 @@
 #include <utility>
 
 #include "k1_fwd_sm.cuh"
+#include "k1_lmhead.cuh"
 
 namespace {
 
@@ -557,6 +561,156 @@ int check_common(const char* fn, const void* logits, int dtype, const Rows& L) {
     return K1_OK;
 }
 
+
+// ---------------------------------------------------------------------------------------
+// LM head fused with K1 (k1_lmhead.cuh): tensor maps, work split, launches
+// ---------------------------------------------------------------------------------------
+using TmapEncodeFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                  const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                  const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+// cuTensorMapEncodeTiled from the driver, looked up through the runtime (no link-time
+// dependency on libcuda).
+int tmap_encoder(TmapEncodeFn* out) {
+    static std::once_flag once;
+    static TmapEncodeFn fn = nullptr;
+    std::call_once(once, [] {
+        void* f = nullptr;
+        cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) ==
+                cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<TmapEncodeFn>(f);
+    });
+    if (!fn) return fail(K1_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
+    *out = fn;
+    return K1_OK;
+}
+
+// Row-major bf16 [rows, cols] matrix read in boxes of box_rows x 64 with 128-byte swizzle.
+int make_tmap(CUtensorMap* m, const void* base, int64_t rows, int64_t cols, int box_rows,
+              const char* what) {
+    TmapEncodeFn enc = nullptr;
+    int rc = tmap_encoder(&enc);
+    if (rc) return rc;
+    const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+    const cuuint64_t strides[1] = {(cuuint64_t)cols * 2};
+    const cuuint32_t box[2] = {(cuuint32_t)k1::lmh::BK, (cuuint32_t)box_rows};
+    const cuuint32_t es[2] = {1, 1};
+    CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides,
+                     box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                     CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(K1_ERR_CUDA, "cuTensorMapEncodeTiled(%s) failed: %d", what, (int)r);
+    return K1_OK;
+}
+
+// Units per row block: the number of runs the vocabulary tiles are cut into.  Chosen among
+// runs of 4 to 32 tiles so that the CTA with the most tiles (units are dealt round robin,
+// in the kernel's unit order) has as few as possible; cached per shape.
+int lmh_parts(int m_blocks, int n_tiles, int grid) {
+    static std::mutex mu;
+    static std::map<std::tuple<int, int, int>, int> cache;
+    const auto key = std::make_tuple(m_blocks, n_tiles, grid);
+    {
+        std::lock_guard<std::mutex> lock(mu);
+        auto it = cache.find(key);
+        if (it != cache.end()) return it->second;
+    }
+    int best = 1;
+    int64_t best_max = INT64_MAX;
+    const int lo = std::max(1, (n_tiles + 31) / 32), hi = std::max(lo, (n_tiles + 3) / 4);
+    std::vector<int64_t> load(grid);
+    for (int np = lo; np <= hi; ++np) {
+        std::fill(load.begin(), load.end(), 0);
+        const int64_t units = (int64_t)m_blocks * np;
+        // unit u -> part: the kernel's order (groups of GROUP_M row blocks, row block fastest)
+        for (int64_t u = 0; u < units; ++u) {
+            const int64_t per_group = (int64_t)k1::lmh::GROUP_M * np;
+            const int64_t g = u / per_group, r = u - g * per_group;
+            const int64_t rows_in_group = std::min<int64_t>(k1::lmh::GROUP_M, m_blocks - g * k1::lmh::GROUP_M);
+            const int64_t part = r / rows_in_group;
+            const int64_t tiles = (part + 1) * n_tiles / np - part * n_tiles / np;
+            load[u % grid] += tiles;
+        }
+        const int64_t mx = *std::max_element(load.begin(), load.end());
+        if (mx < best_max) {
+            best_max = mx;
+            best = np;
+        }
+    }
+    std::lock_guard<std::mutex> lock(mu);
+    cache[key] = best;
+    return best;
+}
+
+struct LmhShape {
+    int m_blocks, n_tiles, k_blocks, grid, n_parts;
+};
+
+int lmh_shape(int64_t n_rows, int64_t hidden, int64_t vocab, int dev, LmhShape* sh) {
+    int sms = 0;
+    int rc = sm_count(dev, &sms);
+    if (rc) return rc;
+    sh->m_blocks = (int)((n_rows + k1::lmh::BM - 1) / k1::lmh::BM);
+    sh->n_tiles = (int)((vocab + k1::lmh::BN - 1) / k1::lmh::BN);
+    sh->k_blocks = (int)((hidden + k1::lmh::BK - 1) / k1::lmh::BK);
+    const int64_t max_units = (int64_t)sh->m_blocks * sh->n_tiles;
+    sh->grid = (int)std::min<int64_t>(sms, max_units);
+    sh->n_parts = lmh_parts(sh->m_blocks, sh->n_tiles, sh->grid);
+    return K1_OK;
+}
+
+size_t lmh_workspace_bytes(int64_t n_rows, const LmhShape& sh) {
+    return (size_t)sh.n_parts * (size_t)n_rows * sizeof(k1::RowPartial) + (size_t)n_rows * sizeof(float) + 256;
+}
+
+int lmh_check(const char* fn, const void* hidden, const void* weight, int64_t n_rows,
+              int64_t hidden_dim, int64_t vocab) {
+    if (!hidden || !weight) return fail(K1_ERR_INVALID_ARGUMENT, "%s: NULL hidden or weight", fn);
+    if (n_rows < 0 || vocab < 1 || hidden_dim < 1)
+        return fail(K1_ERR_INVALID_ARGUMENT, "%s: bad sizes (n_rows %lld, hidden %lld, vocab %lld)", fn,
+                    (long long)n_rows, (long long)hidden_dim, (long long)vocab);
+    if (hidden_dim % 8 != 0)
+        return fail(K1_ERR_INVALID_ARGUMENT, "%s: hidden size must be a multiple of 8 (got %lld)",
+                    fn, (long long)hidden_dim);
+    if ((reinterpret_cast<uintptr_t>(hidden) | reinterpret_cast<uintptr_t>(weight)) % 16 != 0)
+        return fail(K1_ERR_INVALID_ARGUMENT, "%s: hidden and weight must be 16-byte aligned", fn);
+    if (n_rows > ((int64_t)1 << 31) - k1::lmh::BM || vocab > ((int64_t)1 << 31) - k1::lmh::BN)
+        return fail(K1_ERR_INVALID_ARGUMENT, "%s: n_rows and vocab must stay below 2^31", fn);
+    return K1_OK;
+}
+
+template <int MODE>
+int lmh_launch(const char* fn, const void* hidden, const void* weight, int64_t n_rows,
+               int64_t hidden_dim, int64_t vocab, float scale, k1::lmh::Params p,
+               const LmhShape& sh, cudaStream_t s) {
+    CUtensorMap th, tw;
+    int rc = make_tmap(&th, hidden, n_rows, hidden_dim, k1::lmh::BM, "hidden");
+    if (rc) return rc;
+    rc = make_tmap(&tw, weight, vocab, hidden_dim, k1::lmh::BN, "weight");
+    if (rc) return rc;
+    p.n_rows = n_rows;
+    p.vocab = vocab;
+    p.k_blocks = sh.k_blocks;
+    p.m_blocks = sh.m_blocks;
+    p.n_tiles = sh.n_tiles;
+    p.n_parts = sh.n_parts;
+    p.units = sh.m_blocks * sh.n_parts;
+    p.scale = scale;
+    const bool scaled = scale != 1.f;
+    auto kern = scaled ? k1::lmh::k1_lmhead_kernel<MODE, true> : k1::lmh::k1_lmhead_kernel<MODE, false>;
+    int dev = 0;
+    rc = current_device(&dev);
+    if (rc) return rc;
+    int occ = 0;
+    rc = blocks_per_sm(kern, dev, k1::lmh::THREADS, k1::lmh::SMEM_BYTES, &occ);
+    if (rc) return rc;
+    // one CTA per SM: the kernel allocates all of the SM's tensor memory.  Launched without
+    // programmatic dependence, so it never shares an SM with the previous kernel's blocks.
+    kern<<<sh.grid, k1::lmh::THREADS, k1::lmh::SMEM_BYTES, s>>>(th, tw, p);
+    return check_launch(fn);
+}
 }  // namespace
 
 extern "C" {
@@ -860,6 +1014,91 @@ int k1_vocab_shard_backward(const void* logits, int dtype, int64_t n_rows, int64
                          inner_rows, inner_stride, outer_stride, vocab_offset, targets, lse,
                          entropy, g_logp, g_ent, g_lse, d_logits, d_inner_stride,
                          d_outer_stride, stream);
+}
+
+
+size_t k1_lm_head_workspace_bytes(int64_t n_rows, int64_t hidden_dim, int64_t vocab, int device) {
+    if (n_rows < 1 || vocab < 1 || hidden_dim < 1 || device < 0 || device >= kMaxDevices) return 0;
+    LmhShape sh;
+    if (lmh_shape(n_rows, hidden_dim, vocab, device, &sh) != K1_OK) return 0;
+    return lmh_workspace_bytes(n_rows, sh);
+}
+
+int k1_lm_head_forward(const void* hidden, const void* weight, int64_t n_rows, int64_t hidden_dim,
+                       int64_t vocab, float scale, const int64_t* targets, float* logprob,
+                       float* entropy, float* lse, void* logits_out, int64_t logits_stride,
+                       void* workspace, size_t workspace_bytes, void* stream) {
+    static const char* fn = "k1_lm_head_forward";
+    int rc = lmh_check(fn, hidden, weight, n_rows, hidden_dim, vocab);
+    if (rc) return rc;
+    if (n_rows == 0) return K1_OK;
+    if (!targets || !logprob || !entropy || !lse)
+        return fail(K1_ERR_INVALID_ARGUMENT, "%s: NULL targets or output pointer", fn);
+    if (!(scale > 0.f) || !std::isfinite(scale))
+        return fail(K1_ERR_INVALID_ARGUMENT, "%s: scale must be positive and finite", fn);
+    if (logits_out && logits_stride < vocab)
+        return fail(K1_ERR_INVALID_ARGUMENT, "%s: logits_stride must be >= vocab", fn);
+    int dev = 0;
+    rc = current_device(&dev);
+    if (rc) return rc;
+    LmhShape sh;
+    rc = lmh_shape(n_rows, hidden_dim, vocab, dev, &sh);
+    if (rc) return rc;
+    const size_t need = lmh_workspace_bytes(n_rows, sh);
+    if (!workspace || workspace_bytes < need)
+        return fail(K1_ERR_WORKSPACE, "%s: workspace of %zu bytes required (got %zu)", fn, need,
+                    workspace ? workspace_bytes : (size_t)0);
+    if (reinterpret_cast<uintptr_t>(workspace) % 16 != 0)
+        return fail(K1_ERR_INVALID_ARGUMENT, "%s: workspace must be 16-byte aligned", fn);
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    k1::lmh::Params p = {};
+    p.targets = targets;
+    p.part = reinterpret_cast<k1::RowPartial*>(workspace);
+    p.xt = reinterpret_cast<float*>(reinterpret_cast<char*>(workspace) +
+                                    (size_t)sh.n_parts * n_rows * sizeof(k1::RowPartial));
+    p.out = reinterpret_cast<__nv_bfloat16*>(logits_out);
+    p.out_stride = logits_stride;
+    rc = logits_out ? lmh_launch<k1::lmh::STORE>(fn, hidden, weight, n_rows, hidden_dim, vocab,
+                                                 scale, p, sh, s)
+                    : lmh_launch<k1::lmh::STATS>(fn, hidden, weight, n_rows, hidden_dim, vocab,
+                                                 scale, p, sh, s);
+    if (rc) return rc;
+    const int threads = 256;
+    k1::lmh::k1_lmhead_merge_kernel<<<(unsigned)((n_rows + threads - 1) / threads), threads, 0, s>>>(
+        p.part, p.xt, targets, n_rows, vocab, sh.n_parts, logprob, entropy, lse);
+    return check_launch(fn);
+}
+
+int k1_lm_head_backward(const void* hidden, const void* weight, int64_t n_rows, int64_t hidden_dim,
+                        int64_t vocab, float scale, const int64_t* targets, const float* lse,
+                        const float* entropy, const float* g_logp, const float* g_ent,
+                        const float* g_lse, void* d_logits, int64_t d_stride, void* stream) {
+    static const char* fn = "k1_lm_head_backward";
+    int rc = lmh_check(fn, hidden, weight, n_rows, hidden_dim, vocab);
+    if (rc) return rc;
+    if (n_rows == 0) return K1_OK;
+    if (!targets || !lse || !entropy || !d_logits)
+        return fail(K1_ERR_INVALID_ARGUMENT, "%s: NULL targets, lse, entropy or d_logits", fn);
+    if (!(scale > 0.f) || !std::isfinite(scale))
+        return fail(K1_ERR_INVALID_ARGUMENT, "%s: scale must be positive and finite", fn);
+    if (d_stride < vocab) return fail(K1_ERR_INVALID_ARGUMENT, "%s: d_stride must be >= vocab", fn);
+    int dev = 0;
+    rc = current_device(&dev);
+    if (rc) return rc;
+    LmhShape sh;
+    rc = lmh_shape(n_rows, hidden_dim, vocab, dev, &sh);
+    if (rc) return rc;
+    k1::lmh::Params p = {};
+    p.targets = targets;
+    p.lse = lse;
+    p.entropy = entropy;
+    p.g_logp = g_logp;
+    p.g_ent = g_ent;
+    p.g_lse = g_lse;
+    p.out = reinterpret_cast<__nv_bfloat16*>(d_logits);
+    p.out_stride = d_stride;
+    return lmh_launch<k1::lmh::GRAD>(fn, hidden, weight, n_rows, hidden_dim, vocab, scale, p, sh,
+                                     reinterpret_cast<cudaStream_t>(stream));
 }
 
 #ifdef K1_WAIT_TEST

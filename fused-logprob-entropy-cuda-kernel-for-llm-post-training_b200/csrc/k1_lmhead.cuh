@@ -1,0 +1,480 @@
+// k1_lmhead.cuh -- the LM head fused with K1 on B200 tensor cores (tcgen05 + TMEM + TMA).
+//
+// Computes the logits z = bf16(h W^T) of an LM head tile by tile on the 5th-generation
+// tensor cores and folds every tile into K1 in its epilogue, so the forward never writes
+// the [N, V] logits to HBM:
+//   STATS  per-row (m, Z, T) partials of the K1 forward over y = bf16(z * s) (s = 1/T, the
+//          sampling temperature folded in with the rounding of `logits.div_(T)`), plus the
+//          target logit; a small merge kernel turns them into (logprob, entropy, lse);
+//   STORE  the same, and z itself is written (the training path that keeps the logits
+//          for its backward);
+//   GRAD   the K1 backward recomputed from the tile: dz = bf16(bf16(dL/dy) * s), written
+//          in place of the logits (the memory-light training path's backward).
+// The per-element arithmetic of the epilogues is K1's own (fwd_chunk, bwd_vector), applied
+// to the bf16-rounded tile, so z, dz and the statistics are those of K1 on these logits.
+//
+// Kernel layout (one CTA per SM, persistent, 6 warps):
+//   warp 0   TMA producer: 2-D tiled bulk-tensor copies (128-byte swizzle, no cluster
+//            multicast: every load reads this GPU's own memory into this CTA) of a
+//            128 x 64 tile of h and a 256 x 64 tile of W per stage, into a 4-stage ring
+//            of 48 KB (mbarrier complete_tx);
+//   warp 1   MMA issuer: per K block, four tcgen05.mma.cta_group::1.kind::f16
+//            (M = 128, N = 256, K = 16, bf16 x bf16 -> fp32) from shared memory into one
+//            of two 256-column TMEM accumulators; tcgen05.commit releases the stage and,
+//            after the last K block, hands the accumulator to the epilogue;
+//   warps 2-5  epilogue: each thread owns one row of the tile (TMEM lane = row) and reads
+//            its 256 fp32 accumulators 32 columns at a time with tcgen05.ld (32x32b.x32),
+//            while the tensor cores fill the other accumulator.
+// Work is cut into units of (128 rows, a run of consecutive 256-column tiles); the
+// epilogue keeps each row's K1 state in registers across the unit's tiles and writes one
+// partial per row and unit.  Units are ordered in groups of 16 row blocks, row block
+// fastest, so the CTAs running at one time share a few W tiles and one group of h rows in
+// L2 and W is read from HBM about once per group.
+//
+// Every mbarrier wait is bounded (ring::wait, a few seconds at most); a wait that runs out
+// sets bit 3 of k1_ring_error and the CTA stops: the MMA thread waits (bounded) for its
+// issued MMAs, the producer for its issued copies, and the TMEM is freed before exit.
+#pragma once
+
+#include <cuda.h>
+
+#include "k1_ring.cuh"
+
+namespace k1 {
+namespace lmh {
+
+constexpr int BM = 128;               // rows per tile (TMEM lanes)
+constexpr int BN = 256;               // columns per tile (TMEM columns per accumulator)
+constexpr int BK = 64;                // K per stage: 64 bf16 = one 128-byte swizzle row
+constexpr int UK = 16;                // K per tcgen05.mma (kind::f16)
+constexpr int STAGES = 4;
+constexpr int A_BYTES = BM * BK * 2;  // 16 KB
+constexpr int B_BYTES = BN * BK * 2;  // 32 KB
+constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+constexpr int NUM_ACC = 2;
+constexpr int TMEM_COLS = NUM_ACC * BN;  // 512: all of TMEM, so one CTA per SM
+constexpr int EPI_WARPS = 4;
+constexpr int THREADS = (2 + EPI_WARPS) * 32;
+constexpr int GROUP_M = 16;           // row blocks per L2 group
+// Dynamic shared memory: 1 KB of alignment slack, the ring, then the barriers.
+constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + 256;
+
+// tcgen05 instruction descriptor, kind::f16: D fp32 (bits 4-5 = 1), A and B bf16 (bits
+// 7-9 and 10-12 = 1), both K-major (bits 15, 16 = 0), N >> 3 at bits 17-22, M >> 4 at
+// bits 24-28.
+constexpr uint32_t kIdesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) |
+                            ((uint32_t)(BM >> 4) << 24);
+
+enum Mode : int { STATS = 0, STORE = 1, GRAD = 2 };
+
+struct Params {
+    int64_t n_rows, vocab;
+    int k_blocks;     // ceil(hidden / BK); copies beyond `hidden` read zeros
+    int m_blocks;     // ceil(n_rows / BM)
+    int n_tiles;      // ceil(vocab / BN)
+    int n_parts;      // units per row block
+    int units;        // m_blocks * n_parts
+    float scale;      // y = bf16(z * scale) when SCALED
+    const int64_t* targets;
+    RowPartial* part;  // [n_parts][n_rows] (STATS, STORE)
+    float* xt;         // [n_rows]: the target logit, written by the unit holding it
+    // GRAD inputs (per row)
+    const float* lse;
+    const float* entropy;
+    const float* g_logp;
+    const float* g_ent;
+    const float* g_lse;
+    __nv_bfloat16* out;  // STORE: z; GRAD: dz; [n_rows] rows of out_stride elements
+    int64_t out_stride;
+};
+
+// ------------------------------------------------------------------------------------
+// PTX wrappers
+// ------------------------------------------------------------------------------------
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y,
+                                            uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes "
+        "[%0], [%1, {%2, %3}], [%4];" ::"r"(ring::saddr(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(ring::saddr(bar))
+        : "memory");
+}
+
+__device__ __forceinline__ void prefetch_tmap(const CUtensorMap* map) {
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+
+// Shared-memory matrix descriptor of a K-major tile with 128-byte swizzle: start address
+// >> 4 (bits 0-13), leading offset unused (0), stride between 8-row groups 1024 B >> 4
+// (bits 32-45), descriptor version 1 (bits 46-47), layout 2 = 128-byte swizzle (61-63).
+// The tile must start on a 1024-byte boundary; the k-th 16-element slice of the 64-element
+// swizzle row starts 32 k bytes further.
+__device__ __forceinline__ uint64_t smem_desc(uint32_t saddr) {
+    return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)(1024 >> 4) << 32) | (1ull << 46) |
+           (2ull << 61);
+}
+
+__device__ __forceinline__ void umma(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t acc) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+        "l"(da), "l"(db), "r"(kIdesc), "r"(acc));
+}
+
+// Arrive on `bar` once every tcgen05 operation this thread issued so far has completed.
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::
+                     "r"(ring::saddr(bar))
+                 : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() {
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+// 32 consecutive fp32 columns of this thread's TMEM lane (warp-collective).
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+        "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+        "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+          "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]),
+          "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]),
+          "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+          "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]),
+          "=r"(r[31])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// ------------------------------------------------------------------------------------
+// Work decomposition
+// ------------------------------------------------------------------------------------
+struct Unit {
+    int m_blk, part, n0, n1;  // row block, part index, tiles [n0, n1)
+};
+
+__device__ __forceinline__ Unit unit_of(const Params& p, int u) {
+    const int per_group = GROUP_M * p.n_parts;
+    const int g = u / per_group, r = u - g * per_group;
+    const int rows_in_group = min(GROUP_M, p.m_blocks - g * GROUP_M);
+    Unit x;
+    x.part = r / rows_in_group;
+    x.m_blk = g * GROUP_M + (r - x.part * rows_in_group);
+    x.n0 = (int)((int64_t)x.part * p.n_tiles / p.n_parts);
+    x.n1 = (int)((int64_t)(x.part + 1) * p.n_tiles / p.n_parts);
+    return x;
+}
+
+// Bounded wait; on a timeout sets bit 3 of k1_ring_error and the CTA's abort flag.
+__device__ __forceinline__ bool lmh_wait(uint64_t* bar, uint32_t parity, volatile int* abort) {
+    for (int i = 0; i < ring::kMaxTries; ++i) {
+        if (ring::try_wait(bar, parity)) return true;
+        if (*abort) return false;
+    }
+    atomicOr(&k1_ring_error, 8u);
+    *abort = 1;
+    return false;
+}
+
+// ------------------------------------------------------------------------------------
+// Epilogue helpers
+// ------------------------------------------------------------------------------------
+// Round 32 fp32 accumulators to bf16 pairs (the LM head's bf16 logits), columns at or
+// beyond `valid` replaced by the vector padding (lowest finite bf16: e = 0).
+__device__ __forceinline__ void pack_tile_chunk(const uint32_t (&r)[32], int valid,
+                                                uint4 (&v)[4]) {
+    uint32_t w[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+        uint32_t x = DT<__nv_bfloat16>::from_f2(
+            make_float2(__uint_as_float(r[2 * i]), __uint_as_float(r[2 * i + 1])));
+        if (2 * i + 1 >= valid) x = (x & 0x0000FFFFu) | 0xFF7F0000u;
+        if (2 * i >= valid) x = DT<__nv_bfloat16>::kPadWord;
+        w[i] = x;
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) v[u] = make_uint4(w[4 * u], w[4 * u + 1], w[4 * u + 2], w[4 * u + 3]);
+}
+
+// Element k (0..31) of a packed chunk as fp32 (k known at run time: unrolled selects).
+__device__ __forceinline__ float chunk_elem(const uint4 (&v)[4], int k) {
+    uint32_t w = 0;
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+        if ((k >> 3) == u) {
+            const int i = (k >> 1) & 3;
+            w = i == 0 ? v[u].x : i == 1 ? v[u].y : i == 2 ? v[u].z : v[u].w;
+        }
+    }
+    return (k & 1) ? __uint_as_float(w & 0xFFFF0000u) : __uint_as_float(w << 16);
+}
+
+// Store 32 bf16 columns of one row (col0 is a multiple of 32; `valid` columns are real).
+__device__ __forceinline__ void store_chunk(__nv_bfloat16* dst, const uint4 (&v)[4], int valid,
+                                            bool vec_ok) {
+    if (vec_ok && valid >= 32) {
+        uint4* d = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+        for (int u = 0; u < 4; ++u) stg_stream(d + u, v[u]);
+    } else {
+        for (int k = 0; k < 32 && k < valid; ++k) dst[k] = __float2bfloat16_rn(chunk_elem(v, k));
+    }
+}
+
+template <int MODE, bool SCALED>
+__global__ void __launch_bounds__(THREADS, 1)
+    k1_lmhead_kernel(const __grid_constant__ CUtensorMap tmap_h,
+                     const __grid_constant__ CUtensorMap tmap_w, Params p) {
+    extern __shared__ __align__(16) unsigned char lmh_raw[];
+    // 1024-byte aligned ring (128-byte swizzle atoms), barriers after it
+    unsigned char* smem = reinterpret_cast<unsigned char*>(
+        (reinterpret_cast<uintptr_t>(lmh_raw) + 1023) & ~(uintptr_t)1023);
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
+    uint64_t* empty = full + STAGES;
+    uint64_t* tfull = empty + STAGES;
+    uint64_t* tempty = tfull + NUM_ACC;
+    uint64_t* drain = tempty + NUM_ACC;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+    volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; ++s) {
+            ring::bar_init(&full[s], 1);
+            ring::bar_init(&empty[s], 1);
+        }
+        for (int a = 0; a < NUM_ACC; ++a) {
+            ring::bar_init(&tfull[a], 1);
+            ring::bar_init(&tempty[a], EPI_WARPS * 32);
+        }
+        ring::bar_init(drain, 1);
+        *abort = 0;
+        ring::fence_init();
+    }
+    if (warp == 0) {
+        prefetch_tmap(&tmap_h);
+        prefetch_tmap(&tmap_w);
+    }
+    if (warp == 1) {  // the whole warp allocates all of TMEM (one CTA per SM)
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                         ring::saddr(tmem_slot)),
+                     "r"(TMEM_COLS)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    const int G = gridDim.x;
+
+    if (warp == 0) {
+        // ---------------- TMA producer ----------------
+        if (lane == 0) {
+            uint32_t stage = 0, phase = 0, issued = 0;
+            bool ok = true;
+            for (int u = blockIdx.x; ok && u < p.units; u += G) {
+                const Unit x = unit_of(p, u);
+                for (int n = x.n0; ok && n < x.n1; ++n) {
+                    for (int kb = 0; kb < p.k_blocks; ++kb) {
+                        if (!lmh_wait(&empty[stage], phase ^ 1u, abort)) {
+                            ok = false;
+                            break;
+                        }
+                        unsigned char* sa = smem + stage * STAGE_BYTES;
+                        ring::arrive_expect(&full[stage], STAGE_BYTES);
+                        tma_load_2d(sa, &tmap_h, kb * BK, x.m_blk * BM, &full[stage]);
+                        tma_load_2d(sa + A_BYTES, &tmap_w, kb * BK, n * BN, &full[stage]);
+                        ++issued;
+                        if (++stage == STAGES) {
+                            stage = 0;
+                            phase ^= 1u;
+                        }
+                    }
+                }
+            }
+            if (!ok) {
+                // stopping early: wait (bounded) for the copies still in flight
+                for (uint32_t i = (issued > STAGES ? issued - STAGES : 0u); i < issued; ++i)
+                    ring::wait(&full[i % STAGES], (i / STAGES) & 1u);
+            }
+        }
+    } else if (warp == 1) {
+        // ---------------- MMA issuer ----------------
+        if (lane == 0) {
+            uint32_t stage = 0, phase = 0;
+            int t = 0;  // tiles of this CTA so far
+            bool ok = true;
+            const uint32_t sbase = ring::saddr(smem);
+            for (int u = blockIdx.x; ok && u < p.units; u += G) {
+                const Unit x = unit_of(p, u);
+                for (int n = x.n0; ok && n < x.n1; ++n, ++t) {
+                    const int a = t & 1;
+                    if (!lmh_wait(&tempty[a], ((t >> 1) & 1) ^ 1u, abort)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t d = tmem + (uint32_t)(a * BN);
+                    for (int kb = 0; kb < p.k_blocks; ++kb) {
+                        if (!lmh_wait(&full[stage], phase, abort)) {
+                            ok = false;
+                            break;
+                        }
+                        tc_fence_after();
+                        const uint32_t sa = sbase + stage * STAGE_BYTES;
+                        const uint64_t da = smem_desc(sa), db = smem_desc(sa + A_BYTES);
+#pragma unroll
+                        for (int k = 0; k < BK / UK; ++k)  // +32 bytes per K slice: +2 in >> 4 units
+                            umma(d, da + 2 * k, db + 2 * k, (kb > 0 || k > 0) ? 1u : 0u);
+                        umma_commit(&empty[stage]);  // the stage is free once these MMAs ran
+                        if (++stage == STAGES) {
+                            stage = 0;
+                            phase ^= 1u;
+                        }
+                    }
+                    if (ok) umma_commit(&tfull[a]);  // the accumulator is complete
+                }
+            }
+            // every MMA issued has completed before the TMEM can be freed
+            umma_commit(drain);
+            ring::wait(drain, 0);
+        }
+    } else {
+        // ---------------- epilogue (warps 2..5) ----------------
+        const int quarter = warp & 3;  // TMEM lanes 32 quarter .. 32 quarter + 31
+        const int rloc = quarter * 32 + lane;
+        const uint32_t tlane = tmem + ((uint32_t)(quarter * 32) << 16);
+        const bool vec_ok = (p.out_stride & 7) == 0 &&
+                            (reinterpret_cast<uintptr_t>(p.out) & 15) == 0;
+        int t = 0;
+        bool ok = true;
+        for (int u = blockIdx.x; ok && u < p.units; u += G) {
+            const Unit x = unit_of(p, u);
+            const int64_t row = (int64_t)x.m_blk * BM + rloc;
+            const bool live = row < p.n_rows;
+            const int64_t tg = live ? p.targets[row] : -1;
+            const int64_t tcol = (tg >= 0 && tg < p.vocab) ? tg : -1;
+            FwdState st;
+            st.init();
+            float xt = 0.f;
+            bool has_xt = false;
+            BwdRow q;
+            if constexpr (MODE == GRAD) {
+                q.lse = live ? p.lse[row] : 0.f;
+                q.ent = live ? p.entropy[row] : 0.f;
+                q.gl = (live && p.g_logp) ? p.g_logp[row] : 0.f;
+                q.ge = (live && p.g_ent) ? p.g_ent[row] : 0.f;
+                q.gs = (live && p.g_lse) ? p.g_lse[row] : 0.f;
+                q.c0 = q.gs - q.gl - q.ge * q.ent;
+                q.tl = tcol;
+            }
+            for (int n = x.n0; n < x.n1; ++n, ++t) {
+                const int a = t & 1;
+                // warp-uniform: the TMEM loads below are warp-collective
+                if (!__all_sync(0xffffffffu, lmh_wait(&tfull[a], (t >> 1) & 1, abort))) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                for (int c = 0; c < BN / 32; ++c) {
+                    uint32_t r[32];
+                    tmem_ld32(tlane + (uint32_t)(a * BN + c * 32), r);
+                    const int64_t col0 = (int64_t)n * BN + c * 32;
+                    const int64_t left = p.vocab - col0;
+                    const int valid = left < 32 ? (int)left : 32;
+                    if (valid <= 0) continue;
+                    uint4 v[4];
+                    pack_tile_chunk(r, valid, v);
+                    __nv_bfloat16* dst = p.out + row * p.out_stride + col0;
+                    if constexpr (MODE == GRAD) {
+                        uint4 o[4];
+#pragma unroll
+                        for (int k = 0; k < 4; ++k) o[k] = bwd_vector<__nv_bfloat16, SCALED>(v[k], q, p.scale);
+                        if (tcol >= col0 && tcol < col0 + 32) {
+                            const int k = (int)(tcol - col0);
+                            float y = chunk_elem(v, k);
+                            if (SCALED) y = scale1<__nv_bfloat16>(y, p.scale);
+                            const float g = scale1<__nv_bfloat16>(
+                                DT<__nv_bfloat16>::round1(bwd_target_value(y, q)), p.scale);
+                            o[k >> 3] = vec_set<__nv_bfloat16>(o[k >> 3], k & 7, g);
+                        }
+                        if (live) store_chunk(dst, o, valid, vec_ok);
+                    } else {
+                        if constexpr (MODE == STORE) {
+                            if (live) store_chunk(dst, v, valid, vec_ok);
+                        }
+                        if constexpr (SCALED) {
+#pragma unroll
+                            for (int k = 0; k < 4; ++k) {
+                                // padding stays the lowest value (never scaled)
+                                uint4 s = scale_vec<__nv_bfloat16>(v[k], p.scale);
+                                const int b0 = k * 8;
+                                uint32_t* sw = reinterpret_cast<uint32_t*>(&s);
+                                const uint32_t* vw = reinterpret_cast<const uint32_t*>(&v[k]);
+#pragma unroll
+                                for (int i = 0; i < 4; ++i) {
+                                    if (b0 + 2 * i + 1 >= valid) sw[i] = (sw[i] & 0x0000FFFFu) | (vw[i] & 0xFFFF0000u);
+                                    if (b0 + 2 * i >= valid) sw[i] = vw[i];
+                                }
+                                v[k] = s;
+                            }
+                        }
+                        if (tcol >= col0 && tcol < col0 + 32) {
+                            xt = chunk_elem(v, (int)(tcol - col0));
+                            has_xt = true;
+                        }
+                        fwd_chunk<__nv_bfloat16, 4>(v, st, false);
+                    }
+                }
+                tc_fence_before();
+                ring::arrive(&tempty[a]);
+            }
+            if (!ok) break;
+            if constexpr (MODE != GRAD) {
+                if (live) {
+                    RowPartial o;
+                    const bool empty_state = st.m <= DT<__nv_bfloat16>::kLowest;
+                    o.m = empty_state ? -INFINITY : st.m;
+                    o.z = empty_state ? 0.0 : st.z64();
+                    o.t = empty_state ? 0.0 : st.t64();
+                    o.pad = 0.f;
+                    p.part[(int64_t)x.part * p.n_rows + row] = o;
+                    if (has_xt) p.xt[row] = xt;
+                }
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (warp == 1) {
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
+                     "r"(TMEM_COLS)
+                     : "memory");
+    }
+}
+
+// Merge the units' partials of every row (fp64, in part order) and finish the row.
+__global__ void k1_lmhead_merge_kernel(const RowPartial* part, const float* xt,
+                                       const int64_t* targets, int64_t n_rows, int64_t vocab,
+                                       int n_parts, float* logprob, float* entropy, float* lse) {
+    const int64_t row = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (row >= n_rows) return;
+    RowPartial acc;
+    acc.m = -INFINITY;
+    acc.z = acc.t = 0.0;
+    acc.pad = 0.f;
+    for (int i = 0; i < n_parts; ++i) acc = merge_partials(acc, part[(int64_t)i * n_rows + row]);
+    const int64_t tg = targets[row];
+    const double x = (tg >= 0 && tg < vocab) ? (double)xt[row] : 0.0;
+    finalize_row(acc, x, logprob + row, entropy + row, lse + row);
+}
+
+}  // namespace lmh
+}  // namespace k1

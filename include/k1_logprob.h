@@ -226,6 +226,47 @@ int k1_vocab_shard_backward(
     const float* g_lse, void* d_logits, int64_t d_inner_stride, int64_t d_outer_stride,
     void* stream);
 
+/*
+ * LM head fused with K1 on the tensor cores (tcgen05).  The reference names this as its
+ * follow-up and leaves it unbuilt (README.md:135-136, docs/FINAL_REPORT.md:490-494); the
+ * unfused sequence it replaces is the model's LM head GEMM, then the trainer's
+ * `logits.div_(temperature)` and K1 (python/kernel_opt/trainer.py:96-127).
+ *   hidden : n_rows x hidden_dim bf16, row-major (rows hidden_dim elements apart)
+ *   weight : vocab x hidden_dim bf16, row-major (the LM head's [V, H] weight)
+ *   logits : z = bf16(hidden weight^T) (fp32 accumulation), read by K1 as
+ *            y = bf16(z * scale), scale = 1/temperature (1 = no temperature)
+ * hidden_dim must be a multiple of 8 and both matrices 16-byte aligned.
+ *
+ * Workspace bytes k1_lm_head_forward needs (per-row partials of the vocabulary runs);
+ * 0 for invalid arguments.
+ */
+size_t k1_lm_head_workspace_bytes(int64_t n_rows, int64_t hidden_dim, int64_t vocab, int device);
+
+/*
+ * Forward: logprob, entropy, lse (n_rows fp32 each) of K1 on the logits above, computed
+ * tile by tile in the GEMM's epilogue.  logits_out = NULL: the logits never reach memory;
+ * otherwise z is also written to logits_out (rows logits_stride >= vocab elements apart),
+ * for a backward that keeps them.  targets: n_rows int64 (outside [0, vocab): logprob =
+ * -lse, as in K1).
+ */
+int k1_lm_head_forward(const void* hidden, const void* weight, int64_t n_rows, int64_t hidden_dim,
+                       int64_t vocab, float scale, const int64_t* targets, float* logprob,
+                       float* entropy, float* lse, void* logits_out, int64_t logits_stride,
+                       void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * Backward to the logits: recomputes each logits tile on the tensor cores and writes
+ * d_logits = dtype(dtype(dL/dy) * scale), exactly what
+ * k1_fused_logprob_entropy_scaled_backward writes for the logits z (bf16, rows d_stride >=
+ * vocab elements apart), from the forward's lse and entropy and the upstream gradients
+ * (NULL = zero).  The caller then forms dL/dhidden = d_logits weight and
+ * dL/dweight = d_logits^T hidden.
+ */
+int k1_lm_head_backward(const void* hidden, const void* weight, int64_t n_rows, int64_t hidden_dim,
+                        int64_t vocab, float scale, const int64_t* targets, const float* lse,
+                        const float* entropy, const float* g_logp, const float* g_ent,
+                        const float* g_lse, void* d_logits, int64_t d_stride, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -124,3 +124,34 @@ def test_scaled_entry_points_validate_scale(lib):
     assert f(1024, 7, 4, 16, 4, 16, 0, 1.5, 2048, 4096, 4096, 4096, 8192, 1 << 20,
              None) == K1_ERR_DTYPE
     assert f(0, 2, 0, 16, 1, 16, 0, 1.5, 0, 0, 0, 0, 0, 0, None) == K1_OK
+
+
+def test_lm_head_entry_points_validate_before_the_device(lib):
+    """The tensor-core LM head rejects bad sizes, pointers and scales before any device
+    call (so this runs without a GPU)."""
+    i64, p, c_float = ctypes.c_int64, ctypes.c_void_p, ctypes.c_float
+    f = lib.k1_lm_head_forward
+    f.argtypes = [p, p, i64, i64, i64, c_float, p, p, p, p, p, i64, p, ctypes.c_size_t, p]
+    f.restype = ctypes.c_int
+    b = lib.k1_lm_head_backward
+    b.argtypes = [p, p, i64, i64, i64, c_float, p, p, p, p, p, p, p, i64, p]
+    b.restype = ctypes.c_int
+    ok = dict(h=4096, w=8192, n=4, hd=64, v=100, s=1.0)
+
+    def fwd(**kw):
+        a = {**ok, **kw}
+        return f(a["h"], a["w"], a["n"], a["hd"], a["v"], a["s"], 1 << 16, 1 << 17, 1 << 17,
+                 1 << 17, None, a["v"], 1 << 18, 1 << 20, None)
+
+    assert fwd(h=0) == K1_ERR_INVALID and "NULL" in _err(lib)
+    assert fwd(hd=60) == K1_ERR_INVALID and "multiple of 8" in _err(lib)
+    assert fwd(w=8200) == K1_ERR_INVALID and "aligned" in _err(lib)
+    assert fwd(v=0) == K1_ERR_INVALID
+    for s in (0.0, -1.0, float("inf"), float("nan")):
+        assert fwd(s=s) == K1_ERR_INVALID and "scale" in _err(lib)
+    assert fwd(n=0) == K1_OK
+    assert b(4096, 8192, 4, 64, 100, 1.0, 1 << 16, 1 << 17, 1 << 17, None, None, None,
+             1 << 18, 99, None) == K1_ERR_INVALID and "d_stride" in _err(lib)
+    lib.k1_lm_head_workspace_bytes.argtypes = [i64, i64, i64, ctypes.c_int]
+    lib.k1_lm_head_workspace_bytes.restype = ctypes.c_size_t
+    assert lib.k1_lm_head_workspace_bytes(0, 64, 100, 0) == 0
