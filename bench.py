@@ -1107,17 +1107,23 @@ def grpo_arm(args, cfg, rank, local_rank, world):
 
 def lmhead_arm(args, cfg, rank, local_rank, world):
     """LM head fused with K1 (kernel_opt.lm_head) against materialised logits, on config 3's
-    rows and vocabulary with a Qwen2.5-7B-sized hidden state (H = 3584), bf16:
-      fused        -- GEMM in L2-sized row chunks, K1 on each chunk from L2; backward
-                      recomputes each chunk's logits (4 GEMMs per step);
-      materialised -- logits = h W^T ([N, V] in HBM), K1 with the temperature folded in,
-                      autograd (3 GEMMs per step).
-    Both: forward + backward to hidden and weight, and a no-grad forward (the old-policy /
-    reference-policy log-probs of GRPO).  Peak extra device memory of each."""
+    rows and vocabulary with a Qwen2.5-7B-sized hidden state (H = 3584), bf16, T = 0.7:
+      fused        -- tensor-core kernel: the forward folds each logits tile into K1's
+                      statistics in the GEMM epilogue (no [N, V] tensor); the backward
+                      recomputes the tiles chunk by chunk and writes K1's gradient, then
+                      dh / dW by library GEMMs (4 GEMMs per training step);
+      fused_keep   -- the same forward also writing the logits (keep_logits=True); backward
+                      = K1's in-place backward + 2 library GEMMs (3 GEMMs, materialised
+                      memory);
+      materialised -- logits = h W^T (library GEMM), K1 with the temperature folded in,
+                      autograd (3 GEMMs).
+    Training step (forward + backward to hidden and weight) and no-grad forward (the
+    old-policy / reference-policy log-probs of GRPO), peak extra device memory of each, and
+    the fused forward kernel's own TFLOP/s against the library GEMM of the same shape."""
     import torch.distributed as dist
 
     import kernel_opt
-    from kernel_opt import lm_head
+    from kernel_opt import _C, lm_head
 
     device = torch.device("cuda", local_rank)
     torch.cuda.set_device(device)
@@ -1136,16 +1142,18 @@ def lmhead_arm(args, cfg, rank, local_rank, world):
     g_h = torch.full((N,), -0.01 / N, device=device)
     stream = torch.cuda.current_stream(device)
     gemm_flops = 2.0 * N * H * V
+    from kernel_opt import grpo
+    scale = grpo.temperature_scale(T)
 
-    chunk_default = lm_head.default_chunk_rows(N, V, 2)
-    chunk = [chunk_default]
-
-    def fused_step(grad):
+    def fused_step(grad, keep=False):
         hx = h.detach().requires_grad_(grad)
         wx = w.detach().requires_grad_(grad)
-        lp, ent, _ = lm_head.fused_linear_logprob_entropy(hx, wx, t, T, chunk_rows=chunk[0])
+        lp, ent, _ = lm_head.fused_linear_logprob_entropy(hx, wx, t, T, keep_logits=keep)
         if grad:
             torch.autograd.grad((lp, ent), (hx, wx), (g_lp, g_h))
+
+    def fused_keep_step(grad):
+        fused_step(grad, keep=True)
 
     def materialised_step(grad):
         hx = h.detach().requires_grad_(grad)
@@ -1157,7 +1165,8 @@ def lmhead_arm(args, cfg, rank, local_rank, world):
 
     def timed(fn, grad, K):
         for _ in range(max(3, args.warmup)):
-            fn(grad)
+            with torch.set_grad_enabled(grad):
+                fn(grad)
         torch.cuda.synchronize(device)
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         a.record(stream)
@@ -1177,29 +1186,38 @@ def lmhead_arm(args, cfg, rank, local_rank, world):
         torch.cuda.synchronize(device)
         return torch.cuda.max_memory_allocated(device) - base
 
+    # the fused forward kernel alone (statistics only) against the library GEMM alone
+    outs = [torch.empty(N, device=device) for _ in range(3)]
+    zbuf = torch.empty((N, V), dtype=dt, device=device)
+
+    def kernel_only(_grad):
+        _C.lm_head_forward(h, w, t, *outs, scale, None)
+
+    def library_gemm(_grad):
+        torch.mm(h, w.t(), out=zbuf)
+
     K = max(1, min(args.steps, 10))
     with ClockSampler(device) as clocks:
         if world > 1:
             dist.barrier(device_ids=[local_rank])
         fused_ms = timed(fused_step, True, K)
-    res = {
-        "fused_train_ms": fused_ms,
-        "materialised_train_ms": timed(materialised_step, True, K),
-        "fused_nograd_ms": timed(fused_step, False, K),
-        "materialised_nograd_ms": timed(materialised_step, False, K),
-    }
+        res = {
+            "fused_train_ms": fused_ms,
+            "fused_keep_train_ms": timed(fused_keep_step, True, K),
+            "materialised_train_ms": timed(materialised_step, True, K),
+            "fused_nograd_ms": timed(fused_step, False, K),
+            "materialised_nograd_ms": timed(materialised_step, False, K),
+            "fused_forward_kernel_ms": timed(kernel_only, False, K),
+            "library_gemm_ms": timed(library_gemm, False, K),
+        }
+    del zbuf
+    torch.cuda.empty_cache()
     mem = {"fused_train": peak_extra(fused_step, True),
+           "fused_keep_train": peak_extra(fused_keep_step, True),
            "materialised_train": peak_extra(materialised_step, True),
            "fused_nograd": peak_extra(fused_step, False),
            "materialised_nograd": peak_extra(materialised_step, False)}
-    sweep = []
-    for c in (256, 1024, 2048, 4096, 8192):
-        chunk[0] = c
-        sweep.append({"chunk_rows": c, "train_ms": round(timed(fused_step, True, 2), 3),
-                      "nograd_ms": round(timed(fused_step, False, 2), 3),
-                      "train_peak_extra_bytes": peak_extra(fused_step, True)})
-    chunk[0] = chunk_default
-    tt = torch.tensor([fused_ms], device=device, dtype=torch.float64)
+    tt = torch.tensor([res["fused_keep_train_ms"]], device=device, dtype=torch.float64)
     if world > 1:
         dist.all_reduce(tt, op=dist.ReduceOp.MAX)
         dist.barrier(device_ids=[local_rank])
@@ -1213,7 +1231,8 @@ def lmhead_arm(args, cfg, rank, local_rank, world):
             peaks = json.load(f)
     except Exception:
         pass
-    tc_peak = float(peaks.get("bf16_tflops_sustained") or peaks.get("bf16_tflops") or 1400.0)
+    tc_peak = float(peaks.get("bf16_tflops") or 1590.0)
+    kern_tf = gemm_flops / (res["fused_forward_kernel_ms"] / 1e3) / 1e12
     useful = 3 * gemm_flops  # forward logits, dh, dW
     out = {
         "metric": "LM head + K1 fwd+bwd, useful GEMM TFLOP/s (3 GEMMs per step)",
@@ -1223,19 +1242,20 @@ def lmhead_arm(args, cfg, rank, local_rank, world):
         "data": "synthetic",
         "config": {"workload": "LM head [3584 -> 151936] + K1 on config 3's 16 x 1024 rows",
                    "rows": N, "hidden": H, "vocab": V, "temperature": T,
-                   "chunk_rows": chunk_default,
+                   "step": "fused_keep (keep_logits=True) training step",
                    "parallelism": f"row-sharded x{world} (no collective)"},
         "times_ms": {k: round(v, 3) for k, v in res.items()},
-        "speedup_train": round(res["materialised_train_ms"] / res["fused_train_ms"], 3),
+        "speedup_train_keep_vs_materialised": round(res["materialised_train_ms"] / res["fused_keep_train_ms"], 3),
+        "speedup_train_fused_vs_materialised": round(res["materialised_train_ms"] / res["fused_train_ms"], 3),
         "speedup_nograd": round(res["materialised_nograd_ms"] / res["fused_nograd_ms"], 3),
         "peak_extra_bytes": mem,
-        "chunk_sweep": sweep,
-        "roofline": {"bound": "tensor", "achieved": round(4 * gemm_flops / (max_ms / 1e3) / 1e12, 1),
-                     "peak": tc_peak, "unit": "TFLOP/s",
-                     "frac": round(4 * gemm_flops / (max_ms / 1e3) / 1e12 / tc_peak, 4),
-                     "note": "4 GEMMs executed per fused step (incl. the recomputation), "
-                             "library GEMMs; peak = MEASURED_PEAKS.json bf16 sustained"},
-        "gpu_launches": 2 * -(-N // chunk_default) * K,
+        "roofline": {"bound": "tensor", "kernel": "k1_lmhead_kernel (statistics only)",
+                     "achieved": round(kern_tf, 1), "peak": tc_peak, "unit": "TFLOP/s",
+                     "frac": round(kern_tf / tc_peak, 4),
+                     "library_gemm_tflops": round(gemm_flops / (res["library_gemm_ms"] / 1e3) / 1e12, 1),
+                     "note": "2 N H V flops per launch; peak = MEASURED_PEAKS.json bf16 "
+                             "(burst, cuBLAS 8192^3)"},
+        "gpu_launches": 2 * K,
         "clocks": clocks.summary(),
     }
     print(json.dumps(out), flush=True)

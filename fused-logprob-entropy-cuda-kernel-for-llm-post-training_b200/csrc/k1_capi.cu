@@ -644,19 +644,65 @@ int lmh_parts(int m_blocks, int n_tiles, int grid) {
     return best;
 }
 
+// CTA pairs (tcgen05.mma.cta_group::2, 256 x 256 tiles) or single CTAs (128 x 256).
+#ifndef K1_LMH_PAIR
+#define K1_LMH_PAIR 1
+#endif
+
+// Pairs that can be resident at once (a cluster of 2 CTAs of ~200 KB shared memory must
+// fit on two SMs of one GPC): the persistent grid must not exceed it, or part of it would
+// run only after the rest has finished.  Cached per device.
+int lmh_pair_clusters(int dev, int* out) {
+    static std::atomic<int> cache[kMaxDevices];
+    int v = cache[dev].load(std::memory_order_relaxed);
+    if (v == 0) {
+        auto kern = k1::lmh::k1_lmhead_kernel<k1::lmh::STATS, false, true>;
+        const int smem = k1::lmh::Geo<true>::SMEM;
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        if (e != cudaSuccess) return fail(K1_ERR_CUDA, "cudaFuncSetAttribute(smem): %s", cudaGetErrorString(e));
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(2);
+        cfg.blockDim = dim3(k1::lmh::THREADS);
+        cfg.dynamicSmemBytes = (size_t)smem;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = 2;
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        int n = 0;
+        e = cudaOccupancyMaxActiveClusters(&n, kern, &cfg);
+        if (e != cudaSuccess || n < 1)
+            return fail(K1_ERR_CUDA, "cudaOccupancyMaxActiveClusters: %s (%d)", cudaGetErrorString(e), n);
+        v = n;
+        cache[dev].store(v, std::memory_order_relaxed);
+    }
+    *out = v;
+    return K1_OK;
+}
+
 struct LmhShape {
-    int m_blocks, n_tiles, k_blocks, grid, n_parts;
+    int m_blocks, n_tiles, k_blocks, grid, n_parts;  // grid: CTAs, or pairs with PAIR
+    bool pair;
 };
 
 int lmh_shape(int64_t n_rows, int64_t hidden, int64_t vocab, int dev, LmhShape* sh) {
     int sms = 0;
     int rc = sm_count(dev, &sms);
     if (rc) return rc;
-    sh->m_blocks = (int)((n_rows + k1::lmh::BM - 1) / k1::lmh::BM);
+    sh->pair = K1_LMH_PAIR != 0 && sms >= 2;
+    const int tile_m = k1::lmh::BM * (sh->pair ? 2 : 1);
+    sh->m_blocks = (int)((n_rows + tile_m - 1) / tile_m);
     sh->n_tiles = (int)((vocab + k1::lmh::BN - 1) / k1::lmh::BN);
     sh->k_blocks = (int)((hidden + k1::lmh::BK - 1) / k1::lmh::BK);
     const int64_t max_units = (int64_t)sh->m_blocks * sh->n_tiles;
-    sh->grid = (int)std::min<int64_t>(sms, max_units);
+    int slots = sms;
+    if (sh->pair) {
+        rc = lmh_pair_clusters(dev, &slots);
+        if (rc) return rc;
+    }
+    sh->grid = (int)std::min<int64_t>(slots, max_units);
     sh->n_parts = lmh_parts(sh->m_blocks, sh->n_tiles, sh->grid);
     return K1_OK;
 }
@@ -688,7 +734,7 @@ int lmh_launch(const char* fn, const void* hidden, const void* weight, int64_t n
     CUtensorMap th, tw;
     int rc = make_tmap(&th, hidden, n_rows, hidden_dim, k1::lmh::BM, "hidden");
     if (rc) return rc;
-    rc = make_tmap(&tw, weight, vocab, hidden_dim, k1::lmh::BN, "weight");
+    rc = make_tmap(&tw, weight, vocab, hidden_dim, sh.pair ? k1::lmh::BN / 2 : k1::lmh::BN, "weight");
     if (rc) return rc;
     p.n_rows = n_rows;
     p.vocab = vocab;
@@ -699,16 +745,39 @@ int lmh_launch(const char* fn, const void* hidden, const void* weight, int64_t n
     p.units = sh.m_blocks * sh.n_parts;
     p.scale = scale;
     const bool scaled = scale != 1.f;
-    auto kern = scaled ? k1::lmh::k1_lmhead_kernel<MODE, true> : k1::lmh::k1_lmhead_kernel<MODE, false>;
     int dev = 0;
     rc = current_device(&dev);
     if (rc) return rc;
-    int occ = 0;
-    rc = blocks_per_sm(kern, dev, k1::lmh::THREADS, k1::lmh::SMEM_BYTES, &occ);
+    // Launched without programmatic dependence, so it never shares an SM with the previous
+    // kernel's blocks: the kernel allocates all of an SM's tensor memory.
+    auto go = [&](auto kern, bool pair) -> int {
+        const int smem = pair ? k1::lmh::Geo<true>::SMEM : k1::lmh::Geo<false>::SMEM;
+        int occ = 0;
+        int r = blocks_per_sm(kern, dev, k1::lmh::THREADS, (size_t)smem, &occ);
+        if (r) return r;
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3((unsigned)(sh.grid * (pair ? 2 : 1)));
+        cfg.blockDim = dim3(k1::lmh::THREADS);
+        cfg.dynamicSmemBytes = (size_t)smem;
+        cfg.stream = s;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = pair ? 2 : 1;
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = pair ? 1 : 0;
+        cudaError_t e = cudaLaunchKernelEx(&cfg, kern, th, tw, p);
+        if (e != cudaSuccess) return fail(K1_ERR_CUDA, "%s: launch failed: %s", fn, cudaGetErrorString(e));
+        return K1_OK;
+    };
+    if (sh.pair)
+        rc = scaled ? go(k1::lmh::k1_lmhead_kernel<MODE, true, true>, true)
+                    : go(k1::lmh::k1_lmhead_kernel<MODE, false, true>, true);
+    else
+        rc = scaled ? go(k1::lmh::k1_lmhead_kernel<MODE, true, false>, false)
+                    : go(k1::lmh::k1_lmhead_kernel<MODE, false, false>, false);
     if (rc) return rc;
-    // one CTA per SM: the kernel allocates all of the SM's tensor memory.  Launched without
-    // programmatic dependence, so it never shares an SM with the previous kernel's blocks.
-    kern<<<sh.grid, k1::lmh::THREADS, k1::lmh::SMEM_BYTES, s>>>(th, tw, p);
     return check_launch(fn);
 }
 }  // namespace

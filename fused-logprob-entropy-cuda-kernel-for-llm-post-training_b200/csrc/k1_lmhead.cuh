@@ -55,9 +55,14 @@ constexpr int NUM_ACC = 2;
 constexpr int TMEM_COLS = NUM_ACC * BN;  // 512: all of TMEM, so one CTA per SM
 constexpr int EPI_WARPS = 4;
 constexpr int THREADS = (2 + EPI_WARPS) * 32;
-constexpr int GROUP_M = 16;           // row blocks per L2 group
-// Dynamic shared memory: 1 KB of alignment slack, the ring, then the barriers.
-constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + 256;
+#ifndef K1_LMH_CW
+#define K1_LMH_CW 64  // epilogue columns per TMEM wait: 32 or 64
+#endif
+static_assert(K1_LMH_CW == 32 || K1_LMH_CW == 64, "32 or 64 columns per epilogue step");
+#ifndef K1_LMH_GROUP_M
+#define K1_LMH_GROUP_M 16
+#endif
+constexpr int GROUP_M = K1_LMH_GROUP_M;  // row blocks per L2 group
 
 // tcgen05 instruction descriptor, kind::f16: D fp32 (bits 4-5 = 1), A and B bf16 (bits
 // 7-9 and 10-12 = 1), both K-major (bits 15, 16 = 0), N >> 3 at bits 17-22, M >> 4 at
@@ -135,6 +140,29 @@ __device__ __forceinline__ void tc_fence_after() {
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
 }
 
+// 32 consecutive fp32 columns of this thread's TMEM lane (warp-collective); the values
+// may be read only after tmem_wait().
+template <int OFF, int N>
+__device__ __forceinline__ void tmem_ld32_async(uint32_t taddr, uint32_t (&r)[N]) {
+    static_assert(OFF + 32 <= N, "destination too small");
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+        "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+        "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+        : "=r"(r[OFF + 0]), "=r"(r[OFF + 1]), "=r"(r[OFF + 2]), "=r"(r[OFF + 3]), "=r"(r[OFF + 4]),
+          "=r"(r[OFF + 5]), "=r"(r[OFF + 6]), "=r"(r[OFF + 7]), "=r"(r[OFF + 8]), "=r"(r[OFF + 9]),
+          "=r"(r[OFF + 10]), "=r"(r[OFF + 11]), "=r"(r[OFF + 12]), "=r"(r[OFF + 13]),
+          "=r"(r[OFF + 14]), "=r"(r[OFF + 15]), "=r"(r[OFF + 16]), "=r"(r[OFF + 17]),
+          "=r"(r[OFF + 18]), "=r"(r[OFF + 19]), "=r"(r[OFF + 20]), "=r"(r[OFF + 21]),
+          "=r"(r[OFF + 22]), "=r"(r[OFF + 23]), "=r"(r[OFF + 24]), "=r"(r[OFF + 25]),
+          "=r"(r[OFF + 26]), "=r"(r[OFF + 27]), "=r"(r[OFF + 28]), "=r"(r[OFF + 29]),
+          "=r"(r[OFF + 30]), "=r"(r[OFF + 31])
+        : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_wait() {
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
 // 32 consecutive fp32 columns of this thread's TMEM lane (warp-collective).
 __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
     asm volatile(
@@ -184,28 +212,34 @@ __device__ __forceinline__ bool lmh_wait(uint64_t* bar, uint32_t parity, volatil
 // ------------------------------------------------------------------------------------
 // Epilogue helpers
 // ------------------------------------------------------------------------------------
-// Round 32 fp32 accumulators to bf16 pairs (the LM head's bf16 logits), columns at or
+// Round CW fp32 accumulators to bf16 pairs (the LM head's bf16 logits), columns at or
 // beyond `valid` replaced by the vector padding (lowest finite bf16: e = 0).
-__device__ __forceinline__ void pack_tile_chunk(const uint32_t (&r)[32], int valid,
-                                                uint4 (&v)[4]) {
-    uint32_t w[16];
+template <int CW>
+__device__ __forceinline__ void pack_tile_chunk(const uint32_t (&r)[CW], int valid,
+                                                uint4 (&v)[CW / 8]) {
+    uint32_t w[CW / 2];
 #pragma unroll
-    for (int i = 0; i < 16; ++i) {
-        uint32_t x = DT<__nv_bfloat16>::from_f2(
+    for (int i = 0; i < CW / 2; ++i)
+        w[i] = DT<__nv_bfloat16>::from_f2(
             make_float2(__uint_as_float(r[2 * i]), __uint_as_float(r[2 * i + 1])));
-        if (2 * i + 1 >= valid) x = (x & 0x0000FFFFu) | 0xFF7F0000u;
-        if (2 * i >= valid) x = DT<__nv_bfloat16>::kPadWord;
-        w[i] = x;
+    if (valid < CW) {  // the vocabulary's last chunk only
+#pragma unroll
+        for (int i = 0; i < CW / 2; ++i) {
+            if (2 * i + 1 >= valid) w[i] = (w[i] & 0x0000FFFFu) | 0xFF7F0000u;
+            if (2 * i >= valid) w[i] = DT<__nv_bfloat16>::kPadWord;
+        }
     }
 #pragma unroll
-    for (int u = 0; u < 4; ++u) v[u] = make_uint4(w[4 * u], w[4 * u + 1], w[4 * u + 2], w[4 * u + 3]);
+    for (int u = 0; u < CW / 8; ++u)
+        v[u] = make_uint4(w[4 * u], w[4 * u + 1], w[4 * u + 2], w[4 * u + 3]);
 }
 
-// Element k (0..31) of a packed chunk as fp32 (k known at run time: unrolled selects).
-__device__ __forceinline__ float chunk_elem(const uint4 (&v)[4], int k) {
+// Element k (0..CW-1) of a packed chunk as fp32 (k known at run time: unrolled selects).
+template <int NV>
+__device__ __forceinline__ float chunk_elem(const uint4 (&v)[NV], int k) {
     uint32_t w = 0;
 #pragma unroll
-    for (int u = 0; u < 4; ++u) {
+    for (int u = 0; u < NV; ++u) {
         if ((k >> 3) == u) {
             const int i = (k >> 1) & 3;
             w = i == 0 ? v[u].x : i == 1 ? v[u].y : i == 2 ? v[u].z : v[u].w;
@@ -214,43 +248,154 @@ __device__ __forceinline__ float chunk_elem(const uint4 (&v)[4], int k) {
     return (k & 1) ? __uint_as_float(w & 0xFFFF0000u) : __uint_as_float(w << 16);
 }
 
-// Store 32 bf16 columns of one row (col0 is a multiple of 32; `valid` columns are real).
-__device__ __forceinline__ void store_chunk(__nv_bfloat16* dst, const uint4 (&v)[4], int valid,
-                                            bool vec_ok) {
-    if (vec_ok && valid >= 32) {
-        uint4* d = reinterpret_cast<uint4*>(dst);
+// The temperature scale applied to a packed chunk, padding (columns >= valid) left as is
+// (a scaled padding could overflow to -inf).
+template <int NV>
+__device__ __forceinline__ void scale_chunk(uint4 (&v)[NV], int valid, float s) {
+    if (valid == NV * 8) {
 #pragma unroll
-        for (int u = 0; u < 4; ++u) stg_stream(d + u, v[u]);
-    } else {
-        for (int k = 0; k < 32 && k < valid; ++k) dst[k] = __float2bfloat16_rn(chunk_elem(v, k));
+        for (int k = 0; k < NV; ++k) v[k] = scale_vec<__nv_bfloat16>(v[k], s);
+        return;
+    }
+#pragma unroll
+    for (int k = 0; k < NV; ++k) {
+        const uint4 x = scale_vec<__nv_bfloat16>(v[k], s);
+        const int b = k * 8;
+        auto keep = [&](uint32_t scaled, uint32_t orig, int c) -> uint32_t {
+            if (c + 1 >= valid) scaled = (scaled & 0x0000FFFFu) | (orig & 0xFFFF0000u);
+            if (c >= valid) scaled = orig;
+            return scaled;
+        };
+        v[k] = make_uint4(keep(x.x, v[k].x, b), keep(x.y, v[k].y, b + 2), keep(x.z, v[k].z, b + 4),
+                          keep(x.w, v[k].w, b + 6));
     }
 }
 
-template <int MODE, bool SCALED>
+// Store the first `valid` bf16 columns of a packed chunk of one row.
+template <int NV>
+__device__ __forceinline__ void store_chunk(__nv_bfloat16* dst, const uint4 (&v)[NV], int valid,
+                                            bool vec_ok) {
+    if (vec_ok && valid >= NV * 8) {
+        uint4* d = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+        for (int u = 0; u < NV; ++u) stg_stream(d + u, v[u]);
+    } else {
+        for (int k = 0; k < NV * 8 && k < valid; ++k) dst[k] = __float2bfloat16_rn(chunk_elem(v, k));
+    }
+}
+
+// Geometry of the two variants.  PAIR = false: one CTA computes a 128 x 256 tile with
+// tcgen05.mma.cta_group::1 (M = 128) from a 4-stage ring of 48 KB (its 128 rows of h and
+// 256 rows of W per K block).  PAIR = true: a cluster of two CTAs on two SMs computes a
+// 256 x 256 tile with tcgen05.mma.cta_group::2 (M = 256) issued by the first CTA; each
+// CTA holds its 128 rows of h and its 128 rows of W per K block (32 KB; 6 stages), its
+// own 128 x 256 half of the accumulator in its own TMEM, and runs its own epilogue.  The
+// pair moves half the bytes per flop through shared memory and L2 of the single CTA.
+template <bool PAIR>
+struct Geo {
+    static constexpr int CTAS = PAIR ? 2 : 1;
+    static constexpr int TILE_M = BM * CTAS;        // rows per tile (all CTAs of the pair)
+    static constexpr int LOAD_N = BN / CTAS;        // W rows per CTA and K block
+    static constexpr int A_B = BM * BK * 2;         // 16 KB
+    static constexpr int B_B = LOAD_N * BK * 2;     // 32 KB alone, 16 KB in a pair
+    static constexpr int STAGE_B = A_B + B_B;
+#ifndef K1_LMH_PAIR_STAGES
+#define K1_LMH_PAIR_STAGES 6
+#endif
+    static constexpr int NSTAGE = PAIR ? K1_LMH_PAIR_STAGES : STAGES;
+    static constexpr int SMEM = 1024 + NSTAGE * STAGE_B + 256;
+    static constexpr uint32_t IDESC = (1u << 4) | (1u << 7) | (1u << 10) |
+                                      ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(TILE_M >> 4) << 24);
+};
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+// The shared::cluster address of `saddr` (a shared::cta address) in CTA `rank` of the cluster.
+__device__ __forceinline__ uint32_t mapa(uint32_t saddr, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
+    return r;
+}
+// Every thread of both CTAs (per-thread form: the warps need not be converged).
+__device__ __forceinline__ void cluster_sync() {
+    asm volatile("barrier.cluster.arrive.release;\n\tbarrier.cluster.wait.acquire;" ::: "memory");
+}
+// Arrive on an mbarrier of another CTA of the cluster (address from mapa).  The default
+// (CTA-scope) semantics: a release at cluster scope here would make the arriving thread
+// wait for its own bulk copies in flight, which serialises the producer.
+__device__ __forceinline__ void arrive_remote(uint32_t cl_addr) {
+    asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cl_addr) : "memory");
+}
+// Tiled 2-D copy into this CTA's shared memory whose completion is counted on the pair
+// leader's mbarrier (cl_bar, a shared::cluster address).  Not a multicast: each CTA copies
+// only its own tile, from this GPU's memory.
+__device__ __forceinline__ void tma_load_2d_pair(void* dst, const CUtensorMap* map, int x, int y,
+                                                 uint32_t cl_bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes "
+        "[%0], [%1, {%2, %3}], [%4];" ::"r"(ring::saddr(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(cl_bar)
+        : "memory");
+}
+template <bool PAIR>
+__device__ __forceinline__ void umma_t(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t acc) {
+    if constexpr (PAIR) {
+        asm volatile(
+            "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+            "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+            "l"(da), "l"(db), "r"(Geo<true>::IDESC), "r"(acc));
+    } else {
+        umma(tmem_d, da, db, acc);
+    }
+}
+// Arrive on `bar` (this CTA's, or in both CTAs of the pair) once this thread's issued
+// tcgen05 operations have completed.
+template <bool PAIR>
+__device__ __forceinline__ void commit_t(uint64_t* bar) {
+    if constexpr (PAIR) {
+        const uint16_t both = 0x3;
+        asm volatile(
+            "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 "
+            "[%0], %1;" ::"r"(ring::saddr(bar)),
+            "h"(both)
+            : "memory");
+    } else {
+        umma_commit(bar);
+    }
+}
+
+template <int MODE, bool SCALED, bool PAIR>
 __global__ void __launch_bounds__(THREADS, 1)
     k1_lmhead_kernel(const __grid_constant__ CUtensorMap tmap_h,
                      const __grid_constant__ CUtensorMap tmap_w, Params p) {
+    using GE = Geo<PAIR>;
+    constexpr int NST = GE::NSTAGE;
     extern __shared__ __align__(16) unsigned char lmh_raw[];
     // 1024-byte aligned ring (128-byte swizzle atoms), barriers after it
     unsigned char* smem = reinterpret_cast<unsigned char*>(
         (reinterpret_cast<uintptr_t>(lmh_raw) + 1023) & ~(uintptr_t)1023);
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
-    uint64_t* empty = full + STAGES;
-    uint64_t* tfull = empty + STAGES;
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + NST * GE::STAGE_B);
+    uint64_t* empty = full + NST;
+    uint64_t* tfull = empty + NST;
     uint64_t* tempty = tfull + NUM_ACC;
     uint64_t* drain = tempty + NUM_ACC;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
     volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t rank = PAIR ? cluster_rank() : 0u;  // 0: the pair's MMA leader
+    const bool leader = rank == 0;
     if (threadIdx.x == 0) {
-        for (int s = 0; s < STAGES; ++s) {
-            ring::bar_init(&full[s], 1);
+        for (int s = 0; s < NST; ++s) {
+            ring::bar_init(&full[s], GE::CTAS);  // both producers arrive at the leader's
             ring::bar_init(&empty[s], 1);
         }
         for (int a = 0; a < NUM_ACC; ++a) {
             ring::bar_init(&tfull[a], 1);
-            ring::bar_init(&tempty[a], EPI_WARPS * 32);
+            ring::bar_init(&tempty[a], GE::CTAS * EPI_WARPS * 32);  // both epilogues
         }
         ring::bar_init(drain, 1);
         *abort = 0;
@@ -260,25 +405,38 @@ __global__ void __launch_bounds__(THREADS, 1)
         prefetch_tmap(&tmap_h);
         prefetch_tmap(&tmap_w);
     }
-    if (warp == 1) {  // the whole warp allocates all of TMEM (one CTA per SM)
-        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
-                         ring::saddr(tmem_slot)),
-                     "r"(TMEM_COLS)
-                     : "memory");
-        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    if (warp == 1) {  // all of this SM's TMEM (one CTA per SM); in a pair, both CTAs' warps
+        if constexpr (PAIR) {
+            asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                             ring::saddr(tmem_slot)),
+                         "r"(TMEM_COLS)
+                         : "memory");
+            asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+        } else {
+            asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                             ring::saddr(tmem_slot)),
+                         "r"(TMEM_COLS)
+                         : "memory");
+            asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+        }
     }
+    __syncwarp();
     tc_fence_before();
-    __syncthreads();
+    if constexpr (PAIR)
+        cluster_sync();  // the peer's barriers are initialised before any remote arrival
+    else
+        __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
-    const int G = gridDim.x;
+    const int G = gridDim.x / GE::CTAS;        // CTAs (pairs) in the grid
+    const int me = blockIdx.x / GE::CTAS;      // this CTA's (pair's) index
 
     if (warp == 0) {
         // ---------------- TMA producer ----------------
         if (lane == 0) {
             uint32_t stage = 0, phase = 0, issued = 0;
             bool ok = true;
-            for (int u = blockIdx.x; ok && u < p.units; u += G) {
+            for (int u = me; ok && u < p.units; u += G) {
                 const Unit x = unit_of(p, u);
                 for (int n = x.n0; ok && n < x.n1; ++n) {
                     for (int kb = 0; kb < p.k_blocks; ++kb) {
@@ -286,32 +444,44 @@ __global__ void __launch_bounds__(THREADS, 1)
                             ok = false;
                             break;
                         }
-                        unsigned char* sa = smem + stage * STAGE_BYTES;
-                        ring::arrive_expect(&full[stage], STAGE_BYTES);
-                        tma_load_2d(sa, &tmap_h, kb * BK, x.m_blk * BM, &full[stage]);
-                        tma_load_2d(sa + A_BYTES, &tmap_w, kb * BK, n * BN, &full[stage]);
+                        unsigned char* sa = smem + stage * GE::STAGE_B;
+                        const int row_a = x.m_blk * GE::TILE_M + (int)rank * BM;
+                        const int row_b = n * BN + (int)rank * GE::LOAD_N;
+                        if constexpr (PAIR) {
+                            const uint32_t cl = mapa(ring::saddr(&full[stage]), 0);
+                            tma_load_2d_pair(sa, &tmap_h, kb * BK, row_a, cl);
+                            tma_load_2d_pair(sa + GE::A_B, &tmap_w, kb * BK, row_b, cl);
+                            if (leader)
+                                ring::arrive_expect(&full[stage], GE::CTAS * GE::STAGE_B);
+                            else
+                                arrive_remote(cl);
+                        } else {
+                            ring::arrive_expect(&full[stage], GE::STAGE_B);
+                            tma_load_2d(sa, &tmap_h, kb * BK, row_a, &full[stage]);
+                            tma_load_2d(sa + GE::A_B, &tmap_w, kb * BK, row_b, &full[stage]);
+                        }
                         ++issued;
-                        if (++stage == STAGES) {
+                        if (++stage == NST) {
                             stage = 0;
                             phase ^= 1u;
                         }
                     }
                 }
             }
-            if (!ok) {
+            if (!ok && leader) {
                 // stopping early: wait (bounded) for the copies still in flight
-                for (uint32_t i = (issued > STAGES ? issued - STAGES : 0u); i < issued; ++i)
-                    ring::wait(&full[i % STAGES], (i / STAGES) & 1u);
+                for (uint32_t i = (issued > NST ? issued - NST : 0u); i < issued; ++i)
+                    ring::wait(&full[i % NST], (i / NST) & 1u);
             }
         }
     } else if (warp == 1) {
-        // ---------------- MMA issuer ----------------
-        if (lane == 0) {
+        // ---------------- MMA issuer (the pair's leader) ----------------
+        if (lane == 0 && leader) {
             uint32_t stage = 0, phase = 0;
-            int t = 0;  // tiles of this CTA so far
+            int t = 0;  // tiles so far
             bool ok = true;
             const uint32_t sbase = ring::saddr(smem);
-            for (int u = blockIdx.x; ok && u < p.units; u += G) {
+            for (int u = me; ok && u < p.units; u += G) {
                 const Unit x = unit_of(p, u);
                 for (int n = x.n0; ok && n < x.n1; ++n, ++t) {
                     const int a = t & 1;
@@ -327,22 +497,22 @@ __global__ void __launch_bounds__(THREADS, 1)
                             break;
                         }
                         tc_fence_after();
-                        const uint32_t sa = sbase + stage * STAGE_BYTES;
-                        const uint64_t da = smem_desc(sa), db = smem_desc(sa + A_BYTES);
+                        const uint32_t sa = sbase + stage * GE::STAGE_B;
+                        const uint64_t da = smem_desc(sa), db = smem_desc(sa + GE::A_B);
 #pragma unroll
                         for (int k = 0; k < BK / UK; ++k)  // +32 bytes per K slice: +2 in >> 4 units
-                            umma(d, da + 2 * k, db + 2 * k, (kb > 0 || k > 0) ? 1u : 0u);
-                        umma_commit(&empty[stage]);  // the stage is free once these MMAs ran
-                        if (++stage == STAGES) {
+                            umma_t<PAIR>(d, da + 2 * k, db + 2 * k, (kb > 0 || k > 0) ? 1u : 0u);
+                        commit_t<PAIR>(&empty[stage]);  // the stage is free once these MMAs ran
+                        if (++stage == NST) {
                             stage = 0;
                             phase ^= 1u;
                         }
                     }
-                    if (ok) umma_commit(&tfull[a]);  // the accumulator is complete
+                    if (ok) commit_t<PAIR>(&tfull[a]);  // the accumulator is complete
                 }
             }
             // every MMA issued has completed before the TMEM can be freed
-            umma_commit(drain);
+            commit_t<PAIR>(drain);
             ring::wait(drain, 0);
         }
     } else {
@@ -354,9 +524,9 @@ __global__ void __launch_bounds__(THREADS, 1)
                             (reinterpret_cast<uintptr_t>(p.out) & 15) == 0;
         int t = 0;
         bool ok = true;
-        for (int u = blockIdx.x; ok && u < p.units; u += G) {
+        for (int u = me; ok && u < p.units; u += G) {
             const Unit x = unit_of(p, u);
-            const int64_t row = (int64_t)x.m_blk * BM + rloc;
+            const int64_t row = (int64_t)x.m_blk * GE::TILE_M + (int64_t)rank * BM + rloc;
             const bool live = row < p.n_rows;
             const int64_t tg = live ? p.targets[row] : -1;
             const int64_t tcol = (tg >= 0 && tg < p.vocab) ? tg : -1;
@@ -382,58 +552,57 @@ __global__ void __launch_bounds__(THREADS, 1)
                     break;
                 }
                 tc_fence_after();
-                for (int c = 0; c < BN / 32; ++c) {
-                    uint32_t r[32];
-                    tmem_ld32(tlane + (uint32_t)(a * BN + c * 32), r);
-                    const int64_t col0 = (int64_t)n * BN + c * 32;
+                constexpr int CW = K1_LMH_CW;  // columns per step, 32 per TMEM load, one wait
+                for (int c = 0; c < BN / CW; ++c) {
+                    uint32_t r[CW];
+                    __syncwarp();  // converged for the warp-collective TMEM loads
+                    tmem_ld32_async<0>(tlane + (uint32_t)(a * BN + c * CW), r);
+                    if constexpr (CW == 64)
+                        tmem_ld32_async<32 % CW>(tlane + (uint32_t)(a * BN + c * CW + 32), r);
+                    tmem_wait();
+                    const int64_t col0 = (int64_t)n * BN + c * CW;
                     const int64_t left = p.vocab - col0;
-                    const int valid = left < 32 ? (int)left : 32;
+                    const int valid = left < CW ? (int)left : CW;
                     if (valid <= 0) continue;
-                    uint4 v[4];
-                    pack_tile_chunk(r, valid, v);
+                    uint4 v[CW / 8];
+                    pack_tile_chunk<CW>(r, valid, v);
                     __nv_bfloat16* dst = p.out + row * p.out_stride + col0;
                     if constexpr (MODE == GRAD) {
-                        uint4 o[4];
+                        uint4 o[CW / 8];
 #pragma unroll
-                        for (int k = 0; k < 4; ++k) o[k] = bwd_vector<__nv_bfloat16, SCALED>(v[k], q, p.scale);
-                        if (tcol >= col0 && tcol < col0 + 32) {
+                        for (int k = 0; k < CW / 8; ++k) o[k] = bwd_vector<__nv_bfloat16, SCALED>(v[k], q, p.scale);
+                        if (tcol >= col0 && tcol < col0 + CW) {
                             const int k = (int)(tcol - col0);
                             float y = chunk_elem(v, k);
                             if (SCALED) y = scale1<__nv_bfloat16>(y, p.scale);
                             const float g = scale1<__nv_bfloat16>(
                                 DT<__nv_bfloat16>::round1(bwd_target_value(y, q)), p.scale);
-                            o[k >> 3] = vec_set<__nv_bfloat16>(o[k >> 3], k & 7, g);
+#pragma unroll
+                            for (int u = 0; u < CW / 8; ++u)
+                                if ((k >> 3) == u) o[u] = vec_set<__nv_bfloat16>(o[u], k & 7, g);
                         }
                         if (live) store_chunk(dst, o, valid, vec_ok);
                     } else {
                         if constexpr (MODE == STORE) {
                             if (live) store_chunk(dst, v, valid, vec_ok);
                         }
-                        if constexpr (SCALED) {
-#pragma unroll
-                            for (int k = 0; k < 4; ++k) {
-                                // padding stays the lowest value (never scaled)
-                                uint4 s = scale_vec<__nv_bfloat16>(v[k], p.scale);
-                                const int b0 = k * 8;
-                                uint32_t* sw = reinterpret_cast<uint32_t*>(&s);
-                                const uint32_t* vw = reinterpret_cast<const uint32_t*>(&v[k]);
-#pragma unroll
-                                for (int i = 0; i < 4; ++i) {
-                                    if (b0 + 2 * i + 1 >= valid) sw[i] = (sw[i] & 0x0000FFFFu) | (vw[i] & 0xFFFF0000u);
-                                    if (b0 + 2 * i >= valid) sw[i] = vw[i];
-                                }
-                                v[k] = s;
-                            }
-                        }
-                        if (tcol >= col0 && tcol < col0 + 32) {
+                        if constexpr (SCALED) scale_chunk(v, valid, p.scale);
+                        if (tcol >= col0 && tcol < col0 + CW) {
                             xt = chunk_elem(v, (int)(tcol - col0));
                             has_xt = true;
                         }
-                        fwd_chunk<__nv_bfloat16, 4>(v, st, false);
+                        fwd_chunk<__nv_bfloat16, CW / 8>(v, st, false);
                     }
                 }
                 tc_fence_before();
-                ring::arrive(&tempty[a]);
+                if constexpr (PAIR) {
+                    if (leader)
+                        ring::arrive(&tempty[a]);
+                    else
+                        arrive_remote(mapa(ring::saddr(&tempty[a]), 0));
+                } else {
+                    ring::arrive(&tempty[a]);
+                }
             }
             if (!ok) break;
             if constexpr (MODE != GRAD) {
@@ -450,13 +619,23 @@ __global__ void __launch_bounds__(THREADS, 1)
             }
         }
     }
+    __syncwarp();
     tc_fence_before();
-    __syncthreads();
+    if constexpr (PAIR)
+        cluster_sync();  // neither CTA leaves while the pair's MMAs or arrivals may touch it
+    else
+        __syncthreads();
     tc_fence_after();
+    __syncwarp();
     if (warp == 1) {
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
-                     "r"(TMEM_COLS)
-                     : "memory");
+        if constexpr (PAIR)
+            asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem),
+                         "r"(TMEM_COLS)
+                         : "memory");
+        else
+            asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
+                         "r"(TMEM_COLS)
+                         : "memory");
     }
 }
 

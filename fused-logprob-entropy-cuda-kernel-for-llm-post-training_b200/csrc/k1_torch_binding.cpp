@@ -375,6 +375,76 @@ void vocab_shard_backward(at::Tensor logits, at::Tensor targets, int64_t vocab_o
                     d_logits);
 }
 
+// LM head fused with K1 on the tensor cores (bf16 hidden [N, H] and weight [V, H]).
+void check_lm_head(const at::Tensor& hidden, const at::Tensor& weight, const at::Tensor& targets) {
+    TORCH_CHECK(hidden.is_cuda() && weight.is_cuda() && targets.is_cuda(),
+                "hidden, weight and targets must be CUDA");
+    TORCH_CHECK(hidden.scalar_type() == at::kBFloat16 && weight.scalar_type() == at::kBFloat16,
+                "the tensor-core LM head takes bf16 hidden and weight");
+    TORCH_CHECK(hidden.dim() == 2 && weight.dim() == 2 && hidden.size(1) == weight.size(1),
+                "hidden [N, H] and weight [V, H] expected");
+    TORCH_CHECK(hidden.is_contiguous() && weight.is_contiguous(), "hidden and weight must be contiguous");
+    TORCH_CHECK(targets.scalar_type() == at::kLong && targets.is_contiguous() &&
+                    targets.numel() == hidden.size(0),
+                "targets must be contiguous int64 with one entry per hidden row");
+    TORCH_CHECK(hidden.get_device() == weight.get_device() && hidden.get_device() == targets.get_device(),
+                "hidden, weight and targets must be on one device");
+}
+
+void lm_head_forward(at::Tensor hidden, at::Tensor weight, at::Tensor targets, at::Tensor logprob,
+                     at::Tensor entropy, at::Tensor lse_out, double scale,
+                     c10::optional<at::Tensor> logits_out) {
+    check_lm_head(hidden, weight, targets);
+    const int64_t N = hidden.size(0), H = hidden.size(1), V = weight.size(0);
+    for (const at::Tensor* o : {&logprob, &entropy, &lse_out})
+        TORCH_CHECK(o->scalar_type() == at::kFloat && o->is_contiguous() && o->numel() == N,
+                    "outputs must be contiguous fp32 with one entry per row");
+    void* zp = nullptr;
+    int64_t zs = V;
+    if (logits_out.has_value() && logits_out->defined()) {
+        const at::Tensor& z = *logits_out;
+        TORCH_CHECK(z.scalar_type() == at::kBFloat16 && z.dim() == 2 && z.size(0) == N &&
+                        z.size(1) == V && z.stride(1) == 1,
+                    "logits_out must be bf16 [N, V] with unit stride along V");
+        zp = z.data_ptr();
+        zs = z.stride(0);
+    }
+    if (N == 0) return;
+    c10::cuda::CUDAGuard guard(hidden.device());
+    const size_t ws_bytes = k1_lm_head_workspace_bytes(N, H, V, hidden.get_device());
+    TORCH_CHECK(ws_bytes > 0, "k1: could not size the LM head workspace: ", k1_last_error());
+    at::Tensor ws = at::empty({(int64_t)ws_bytes}, hidden.options().dtype(at::kByte));
+    check_launch(k1_lm_head_forward(hidden.data_ptr(), weight.data_ptr(), N, H, V, (float)scale,
+                                    targets.data_ptr<int64_t>(), logprob.data_ptr<float>(),
+                                    entropy.data_ptr<float>(), lse_out.data_ptr<float>(), zp, zs,
+                                    ws.data_ptr(), ws_bytes,
+                                    at::cuda::getCurrentCUDAStream().stream()));
+}
+
+void lm_head_backward(at::Tensor hidden, at::Tensor weight, at::Tensor targets, at::Tensor lse,
+                      at::Tensor entropy, c10::optional<at::Tensor> g_logp,
+                      c10::optional<at::Tensor> g_ent, c10::optional<at::Tensor> g_lse,
+                      at::Tensor d_logits, double scale) {
+    check_lm_head(hidden, weight, targets);
+    const int64_t N = hidden.size(0), H = hidden.size(1), V = weight.size(0);
+    TORCH_CHECK(lse.scalar_type() == at::kFloat && entropy.scalar_type() == at::kFloat &&
+                    lse.is_contiguous() && entropy.is_contiguous() && lse.numel() == N &&
+                    entropy.numel() == N,
+                "saved lse / entropy must be contiguous fp32 with one entry per row");
+    TORCH_CHECK(d_logits.scalar_type() == at::kBFloat16 && d_logits.dim() == 2 &&
+                    d_logits.size(0) == N && d_logits.size(1) == V && d_logits.stride(1) == 1,
+                "d_logits must be bf16 [N, V] with unit stride along V");
+    const float* gl = opt_grad(g_logp, N, hidden);
+    const float* ge = opt_grad(g_ent, N, hidden);
+    const float* gs = opt_grad(g_lse, N, hidden);
+    if (N == 0) return;
+    c10::cuda::CUDAGuard guard(hidden.device());
+    check_launch(k1_lm_head_backward(hidden.data_ptr(), weight.data_ptr(), N, H, V, (float)scale,
+                                     targets.data_ptr<int64_t>(), lse.data_ptr<float>(),
+                                     entropy.data_ptr<float>(), gl, ge, gs, d_logits.data_ptr(),
+                                     d_logits.stride(0), at::cuda::getCurrentCUDAStream().stream()));
+}
+
 }  // namespace
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -400,6 +470,19 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
           "Vocab-parallel: per-row partial state of a vocabulary shard.");
     m.def("vocab_combine", &vocab_combine, "Vocab-parallel: merge gathered shard partials.");
     m.def("vocab_shard_backward", &vocab_shard_backward, "Vocab-parallel: backward of a shard.");
+    m.def("lm_head_forward", &lm_head_forward,
+          "LM head fused with K1 on the tensor cores: per-row logprob / entropy / lse of "
+          "bf16(hidden weight^T) read as bf16(z * scale); optionally also writes z.",
+          pybind11::arg("hidden"), pybind11::arg("weight"), pybind11::arg("targets"),
+          pybind11::arg("logprob"), pybind11::arg("entropy"), pybind11::arg("lse_out"),
+          pybind11::arg("scale"), pybind11::arg("logits_out") = pybind11::none());
+    m.def("lm_head_backward", &lm_head_backward,
+          "Recomputes the LM head's logits on the tensor cores and writes K1's gradient "
+          "w.r.t. them (the scaled backward's rounding).",
+          pybind11::arg("hidden"), pybind11::arg("weight"), pybind11::arg("targets"),
+          pybind11::arg("lse"), pybind11::arg("entropy"), pybind11::arg("g_logp"),
+          pybind11::arg("g_ent"), pybind11::arg("g_lse"), pybind11::arg("d_logits"),
+          pybind11::arg("scale"));
     m.def("abi_version", &k1_abi_version, "C ABI version of the loaded libk1_b200.so.");
     m.def(
         "ring_status",

@@ -3,24 +3,27 @@
 The reference computes K1 on logits that the model has already materialised
 (`model(**inputs).logits`, python/kernel_opt/trainer.py:96); it names fusing the LM-head
 projection with K1 as the follow-up that would remove that tensor (README.md:135-136,
-docs/FINAL_REPORT.md:490-494).  Here the projection runs in row chunks: each chunk's
-logits are produced by the GEMM into one reused buffer and consumed there by the K1
-kernels, so device memory holds one chunk of logits, not N x V (and no N x V gradient).
+docs/FINAL_REPORT.md:490-494).
 
-  forward   per chunk:  z = h_c W^T  ->  K1 forward (temperature applied in-kernel)
-  backward  per chunk:  z = h_c W^T (recomputed)  ->  K1 backward in place (z <- dL/dz)
-                        dh_c = dz W,   dW += dz^T h_c  (fp32 accumulator)
+bf16 heads (the training case) run on the tensor-core kernel of csrc/k1_lmhead.cuh
+(`_C.lm_head_forward` / `_C.lm_head_backward`): a tcgen05 GEMM whose epilogue folds every
+128 x 256 tile of the logits straight into K1's per-row statistics, so the forward never
+writes the logits to memory, and whose backward mode recomputes the tiles and writes K1's
+gradient w.r.t. them.
 
-The GEMMs are plain library GEMMs (cuBLAS through torch.mm / addmm); dW accumulates in
-fp32 across chunks inside the GEMM (`addmm(..., out_dtype=float32)`), so its rounding
-matches one unchunked GEMM with fp32 accumulation up to summation order.  The backward
-spends one extra GEMM (the recomputation) to avoid storing the logits.
+  forward           z = bf16(h W^T), K1 statistics of bf16(z / T) in the GEMM epilogue
+  backward          per row chunk: dz = K1 gradient from the recomputed tiles (tensor
+                    cores), then dh_c = dz W, dW += dz^T h_c (library GEMMs, fp32 dW)
+  keep_logits=True  the forward also writes z; the backward is K1's in-place backward on
+                    it and two library GEMMs (memory of materialised logits, one GEMM less)
 
-Chunk size.  Every chunk's GEMMs stream the whole weight (V x H) and read and write the
-whole fp32 dW accumulator, so small chunks turn the GEMMs memory-bound: at V = 151936,
-H = 3584 a chunk small enough for its logits to stay in the 126 MB L2 (192 rows) makes a
-training step 3x slower than materialised logits.  Chunks are therefore sized by a memory
-budget for the logits buffer (default 1 GiB), in multiples of 256 rows, and equalised.
+Other dtypes (fp16, fp32) keep the composition of library GEMMs and K1 kernels on row
+chunks: each chunk's logits are produced into one reused buffer and consumed there by K1.
+
+Chunk size (the backward's dz buffer, and the whole path for other dtypes) is a memory
+budget (default 1 GiB), in multiples of 256 rows and equalised: every chunk's GEMMs
+stream all of W and read and write the fp32 dW accumulator, so chunks small enough to
+stay in L2 would make the GEMMs memory-bound.
 """
 from __future__ import annotations
 
@@ -113,6 +116,67 @@ class _LinearLogprobEntropy(torch.autograd.Function):
         return dh, dw, None, None, None
 
 
+def tensor_core_head(hidden: torch.Tensor, weight: torch.Tensor) -> bool:
+    """Whether the tcgen05 kernel serves this head: bf16 [N, H] x [V, H], H % 8 == 0."""
+    return (hidden.dtype == torch.bfloat16 and weight.dtype == torch.bfloat16 and
+            hidden.is_cuda and weight.is_cuda and hidden.shape[-1] % 8 == 0)
+
+
+class _TCLinearLogprobEntropy(torch.autograd.Function):
+    """The tensor-core path (bf16).  See the module docstring."""
+
+    @staticmethod
+    def forward(ctx, hidden, weight, targets, scale, chunk_rows, keep_logits):
+        N, V = hidden.shape[0], weight.shape[0]
+        targets = targets.contiguous()
+        logprob, entropy, lse = _alloc_outputs(targets)
+        grad = ctx.needs_input_grad[0] or ctx.needs_input_grad[1]
+        z = torch.empty((N, V), dtype=hidden.dtype, device=hidden.device) \
+            if (keep_logits and grad) else None
+        _C.lm_head_forward(hidden, weight, targets, logprob, entropy, lse, scale, z)
+        ctx.save_for_backward(hidden, weight, targets, lse, entropy,
+                              z if z is not None else lse.new_empty(0))
+        ctx.keep = z is not None
+        ctx.scale = scale
+        ctx.chunk_rows = min(max(1, N), chunk_rows)
+        ctx.set_materialize_grads(False)
+        ctx.mark_non_differentiable(lse)
+        return logprob, entropy, lse
+
+    @staticmethod
+    def backward(ctx, g_logp, g_ent, _g_lse):
+        hidden, weight, targets, lse, entropy, z = ctx.saved_tensors
+        need_h, need_w = ctx.needs_input_grad[0], ctx.needs_input_grad[1]
+        if (g_logp is None and g_ent is None) or not (need_h or need_w):
+            return None, None, None, None, None, None
+        gl = None if g_logp is None else g_logp.to(torch.float32).contiguous()
+        ge = None if g_ent is None else g_ent.to(torch.float32).contiguous()
+        if ctx.keep:
+            # K1's backward in place on the kept logits, then the two library GEMMs that
+            # autograd would run for z = h W^T
+            _C.fused_logprob_entropy_scaled_backward(z, targets, lse, entropy, gl, ge, None, z,
+                                                     ctx.scale)
+            dh = torch.mm(z, weight) if need_h else None
+            dw = torch.mm(z.t(), hidden) if need_w else None
+            return dh, dw, None, None, None, None
+        N, V = hidden.shape[0], weight.shape[0]
+        c = ctx.chunk_rows
+        dz = torch.empty((c, V), dtype=hidden.dtype, device=hidden.device)
+        dh = torch.empty_like(hidden) if need_h else None
+        dw32 = torch.zeros(weight.shape, dtype=torch.float32, device=weight.device) if need_w else None
+        for a, b in _chunks(N, c):
+            d = dz[: b - a]
+            _C.lm_head_backward(hidden[a:b], weight, targets[a:b], lse[a:b], entropy[a:b],
+                                None if gl is None else gl[a:b], None if ge is None else ge[a:b],
+                                None, d, ctx.scale)
+            if need_h:
+                torch.mm(d, weight, out=dh[a:b])
+            if need_w:
+                torch.addmm(dw32, d.t(), hidden[a:b], out_dtype=torch.float32, out=dw32)
+        dw = dw32.to(weight.dtype) if need_w else None
+        return dh, dw, None, None, None, None
+
+
 # Config attributes that make the logits something other than hidden @ W^T
 _LOGIT_TRANSFORMS = ("final_logit_softcapping", "logit_scale", "logits_scaling",
                      "output_multiplier_scale")
@@ -136,17 +200,21 @@ def fused_head_parts(model):
 
 def fused_linear_logprob_entropy(hidden: torch.Tensor, weight: torch.Tensor,
                                  targets: torch.Tensor, temperature: float = 1.0,
-                                 chunk_rows: int | None = None):
+                                 chunk_rows: int | None = None, keep_logits: bool = False):
     """Per-row log-prob of `targets`, entropy and log-sum-exp of
-    softmax((hidden @ weight.T) / temperature), with gradients to `hidden` and `weight`,
-    never holding more than one chunk of logits (`chunk_rows` rows; default: the fewest
-    equal chunks of at most 1 GiB of logits).
+    softmax((hidden @ weight.T) / temperature), with gradients to `hidden` and `weight`.
 
     hidden: [..., H], weight: [V, H] (an nn.Linear's weight, no bias), same dtype;
     targets: [...] int64 (ignore index -100 allowed).  Returns (logprob, entropy, lse)
     shaped like `targets`.  The logits are rounded to the weight's dtype (as a model's
     logits are) and divided by the temperature with the rounding of an in-place
     `div_(temperature)`, so results equal K1 on the materialised, divided logits.
+
+    bf16 heads run on the tensor-core kernel: the forward never writes the logits; the
+    backward recomputes them chunk by chunk (`chunk_rows` rows of gradient at a time;
+    default: the fewest equal chunks of at most 1 GiB).  `keep_logits=True` trades memory
+    for time: the forward also writes the [N, V] logits and the backward reuses them.
+    Other dtypes run library GEMMs and K1 kernels on row chunks.
     """
     lead = targets.shape
     h2 = hidden.reshape(-1, hidden.shape[-1])
@@ -154,5 +222,10 @@ def fused_linear_logprob_entropy(hidden: torch.Tensor, weight: torch.Tensor,
         h2 = h2.contiguous()
     t1 = targets.reshape(-1)
     c = chunk_rows or default_chunk_rows(h2.shape[0], weight.shape[0], weight.element_size())
-    lp, h, l = _LinearLogprobEntropy.apply(h2, weight, t1, temperature_scale(temperature), c)
+    scale = temperature_scale(temperature)
+    if tensor_core_head(h2, weight):
+        w = weight if weight.is_contiguous() else weight.contiguous()
+        lp, h, l = _TCLinearLogprobEntropy.apply(h2, w, t1, scale, c, bool(keep_logits))
+    else:
+        lp, h, l = _LinearLogprobEntropy.apply(h2, weight, t1, scale, c)
     return lp.view(lead), h.view(lead), l.view(lead)
