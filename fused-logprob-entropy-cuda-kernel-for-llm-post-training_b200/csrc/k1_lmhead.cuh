@@ -13,19 +13,23 @@
 // The per-element arithmetic of the epilogues is K1's own (fwd_chunk, bwd_vector), applied
 // to the bf16-rounded tile, so z, dz and the statistics are those of K1 on these logits.
 //
-// Kernel layout (one CTA per SM, persistent, 6 warps):
-//   warp 0   TMA producer: 2-D tiled bulk-tensor copies (128-byte swizzle, no cluster
-//            multicast: every load reads this GPU's own memory into this CTA) of a
-//            128 x 64 tile of h and a 256 x 64 tile of W per stage, into a 4-stage ring
-//            of 48 KB (mbarrier complete_tx);
-//   warp 1   MMA issuer: per K block, four tcgen05.mma.cta_group::1.kind::f16
-//            (M = 128, N = 256, K = 16, bf16 x bf16 -> fp32) from shared memory into one
-//            of two 256-column TMEM accumulators; tcgen05.commit releases the stage and,
-//            after the last K block, hands the accumulator to the epilogue;
-//   warps 2-5  epilogue: each thread owns one row of the tile (TMEM lane = row) and reads
-//            its 256 fp32 accumulators 32 columns at a time with tcgen05.ld (32x32b.x32),
-//            while the tensor cores fill the other accumulator.
-// Work is cut into units of (128 rows, a run of consecutive 256-column tiles); the
+// Kernel layout (one CTA per SM, persistent, 6 warps).  The default variant runs CTA
+// pairs (a cluster of 2 CTAs on 2 SMs, tcgen05.mma.cta_group::2): each pair computes a
+// 256 x 256 tile of the logits, each CTA holding its 128 rows of h and 128 rows of W per
+// K block and its 128 x 256 half of the accumulator; the single-CTA variant (K1_LMH_PAIR=0)
+// computes 128 x 256 tiles alone.
+//   warp 0   TMA producer: 2-D tiled bulk-tensor copies (128-byte swizzle; every copy
+//            reads this GPU's own memory into this CTA's own shared memory) of 64-wide
+//            K blocks of h and W into a ring (pair: 6 stages of 32 KB; single: 4 of
+//            48 KB), completion counted on the pair leader's mbarrier;
+//   warp 1   MMA issuer (the pair's first CTA): per K block, four tcgen05.mma of kind::f16
+//            (bf16 x bf16 -> fp32, K = 16 each) from shared memory into one of two
+//            256-column TMEM accumulators; tcgen05.commit releases the stage in both CTAs
+//            and, after the last K block, hands the accumulator to both epilogues;
+//   warps 2-5  epilogue: each thread owns one row of its CTA's half tile (TMEM lane = row)
+//            and reads its 256 fp32 accumulators 64 columns per wait with tcgen05.ld
+//            (32x32b.x32), while the tensor cores fill the other accumulator.
+// Work is cut into units of (a tile's rows, a run of consecutive 256-column tiles); the
 // epilogue keeps each row's K1 state in registers across the unit's tiles and writes one
 // partial per row and unit.  Units are ordered in groups of 16 row blocks, row block
 // fastest, so the CTAs running at one time share a few W tiles and one group of h rows in
@@ -330,7 +334,7 @@ __device__ __forceinline__ void arrive_remote(uint32_t cl_addr) {
     asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cl_addr) : "memory");
 }
 // Tiled 2-D copy into this CTA's shared memory whose completion is counted on the pair
-// leader's mbarrier (cl_bar, a shared::cluster address).  Not a multicast: each CTA copies
+// leader's mbarrier (cl_bar, a shared::cluster address).  Each CTA copies
 // only its own tile, from this GPU's memory.
 __device__ __forceinline__ void tma_load_2d_pair(void* dst, const CUtensorMap* map, int x, int y,
                                                  uint32_t cl_bar) {

@@ -154,15 +154,16 @@ def _tc_forward(h, w, t, scale, keep=True):
 @pytest.mark.parametrize("shape", TC_SHAPES)
 def test_tc_logits_are_the_rounded_product(shape):
     """z = bf16 of the fp32-accumulated product: within one bf16 ulp of the exact (fp64)
-    product everywhere, and nearly always the library GEMM's bits (both round the same
-    fp32 sums, up to summation order)."""
+    product plus the fp32 accumulation error (2^-20 of the sum of |h_k w_k|, which matters
+    only for logits near zero).  (The library GEMM rounds fp32 sums taken in another
+    order -- split over K for few rows -- so its bits are not the reference here.)"""
     h, w, t = _tc_problem(*shape, seed=10)
     _, z = _tc_forward(h, w, t, 1.0)
     exact = h.double() @ w.double().t()
     _, e = torch.frexp(exact)
     ulp = torch.ldexp(torch.ones_like(exact), e - 8)  # bf16: 8 significant bits
-    assert bool(((z.double() - exact).abs() <= ulp).all()), "a logit is off by more than 1 ulp"
-    assert float((z != torch.mm(h, w.t())).float().mean()) < 1e-2
+    acc = (h.double().abs() @ w.double().abs().t()) * 2.0 ** -20
+    assert bool(((z.double() - exact).abs() <= ulp + acc).all()), "a logit is off by > 1 ulp"
 
 
 @pytest.mark.parametrize("shape", TC_SHAPES)
