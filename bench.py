@@ -1132,6 +1132,10 @@ def lmhead_arm(args, cfg, rank, local_rank, world):
                                 timeout=datetime.timedelta(seconds=300))
     B, S, V, H = 16, 1024, 151936, 3584
     N = B * S
+    if args.lmh_rows:
+        N = args.lmh_rows
+    if args.lmh_vocab:
+        V = args.lmh_vocab
     dt = torch.bfloat16
     T = 0.7
     gen = torch.Generator(device=device).manual_seed(99 + rank)
@@ -1240,7 +1244,8 @@ def lmhead_arm(args, cfg, rank, local_rank, world):
         "n_gpus": world, "steps": K, "warmup": max(3, args.warmup), "ms_per_step": round(max_ms, 3),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic",
-        "config": {"workload": "LM head [3584 -> 151936] + K1 on config 3's 16 x 1024 rows",
+        "config": {"workload": (f"LM head [{H} -> {V}] + K1 on {N} rows" if (args.lmh_rows or args.lmh_vocab)
+                                else "LM head [3584 -> 151936] + K1 on config 3's 16 x 1024 rows"),
                    "rows": N, "hidden": H, "vocab": V, "temperature": T,
                    "step": "fused_keep (keep_logits=True) training step",
                    "parallelism": f"row-sharded x{world} (no collective)"},
@@ -1350,6 +1355,10 @@ def main():
                     help="skip the config 3 / config 4 kernel legs of the N = 1 line")
     ap.add_argument("--no-vocab-parallel", action="store_true",
                     help="skip the config 5 vocab-parallel sub-record")
+    ap.add_argument("--lmh-rows", type=int, default=0,
+                    help="--mode lmhead: rows (default 16384; smaller for profiling)")
+    ap.add_argument("--lmh-vocab", type=int, default=0,
+                    help="--mode lmhead: vocabulary (default 151936; smaller for profiling)")
     ap.add_argument("--eager", action="store_true",
                     help="time eager steps only (no CUDA-graph replay of the step)")
     ap.add_argument("--mode", choices=["rows", "vocab", "grpo", "lmhead"], default="rows",
