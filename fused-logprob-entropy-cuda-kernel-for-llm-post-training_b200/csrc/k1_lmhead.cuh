@@ -63,6 +63,9 @@ constexpr int THREADS = (2 + EPI_WARPS) * 32;
 #define K1_LMH_CW 64  // epilogue columns per TMEM wait: 32 or 64
 #endif
 static_assert(K1_LMH_CW == 32 || K1_LMH_CW == 64, "32 or 64 columns per epilogue step");
+#ifndef K1_LMH_PREFETCH
+#define K1_LMH_PREFETCH 0  // 1: prefetch the next tile's W into L2 while loading this one
+#endif
 #ifndef K1_LMH_GROUP_M
 #define K1_LMH_GROUP_M 16
 #endif
@@ -107,6 +110,14 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, i
         "[%0], [%1, {%2, %3}], [%4];" ::"r"(ring::saddr(dst)),
         "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(ring::saddr(bar))
         : "memory");
+}
+
+// Ask L2 to fetch a tile of the tensor (nothing lands in shared memory).
+__device__ __forceinline__ void tma_prefetch_l2(const CUtensorMap* map, int x, int y) {
+    asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global [%0, {%1, %2}];" ::"l"(
+                     reinterpret_cast<uint64_t>(map)),
+                 "r"(x), "r"(y)
+                 : "memory");
 }
 
 __device__ __forceinline__ void prefetch_tmap(const CUtensorMap* map) {
@@ -464,6 +475,9 @@ __global__ void __launch_bounds__(THREADS, 1)
                             tma_load_2d(sa, &tmap_h, kb * BK, row_a, &full[stage]);
                             tma_load_2d(sa + GE::A_B, &tmap_w, kb * BK, row_b, &full[stage]);
                         }
+                        // the next tile's W rows of this K block into L2, a tile ahead
+                        if (K1_LMH_PREFETCH && n + 1 < x.n1)
+                            tma_prefetch_l2(&tmap_w, kb * BK, row_b + BN);
                         ++issued;
                         if (++stage == NST) {
                             stage = 0;

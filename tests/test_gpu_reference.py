@@ -69,3 +69,27 @@ def test_reference_edge_semantics_are_followed():
     for r, o in zip(ref, ours):
         assert_close_nan(o, r, 1e-4, 1e-4, "edge")
     np.testing.assert_array_equal(np.isfinite(ref[0]), np.isfinite(ours[0]))
+
+
+@needs_ref
+def test_minus_inf_logits_gradient_deliberately_differs():
+    """The one deliberate difference from the reference: at a -inf logit the reference's
+    backward computes 0 * inf = NaN (p = 0 times (x - lse) = -inf), where this build writes
+    0, the limit of the gradient.  Everywhere else in the row both agree."""
+    V = 2048
+    x = seeded_logits((3, V), torch.float32, 2.0, seed=31)
+    x[1, ::8] = float("-inf")
+    t = torch.tensor([5, 9, 700])
+    g = [a.cuda() for a in grads_like((3,), seed=32)]
+    xg, tg = x.cuda(), t.cuda()
+    lp, h, l = reference_k1.forward(xg, tg)
+    ref = reference_k1.backward(xg, tg, l, h, *g).cpu()
+    xo = xg.clone().requires_grad_(True)
+    (ours,) = torch.autograd.grad(kernel_opt.fused_logprob_entropy(xo, tg), xo, g)
+    ours = ours.cpu()
+    neg = torch.isinf(x) & (x < 0)
+    assert torch.isnan(ref[neg]).all(), "the reference no longer returns NaN at -inf logits"
+    assert (ours[neg] == 0).all()
+    keep = ~neg
+    assert_close_nan(ours[keep].double().numpy(), ref[keep].double().numpy(), 1e-4, 1e-4,
+                     "d_logits away from the -inf entries")
