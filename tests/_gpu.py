@@ -65,8 +65,11 @@ def check_grad(d, logits_cpu, targets_cpu, g_logp=None, g_ent=None, g_lse=None, 
         t = np.asarray(targets_cpu, np.int64).reshape(rows)
         onehot = (np.arange(x.shape[-1]) == t[..., None])
         terms = terms + onehot * np.abs(gl)[..., None]
+    # below the dtype's smallest normal number the output format itself has no relative
+    # precision (fp16 subnormals): the absolute floor covers those
+    tiny = float(torch.finfo(dt).tiny)
     plain = finite & np.isfinite(got) & (d0 != 0) & np.isfinite(terms) & \
-        (np.abs(d0) >= terms / 20.0) & (np.abs(d0) >= GRAD_FLOOR[dt])
+        (np.abs(d0) >= terms / 20.0) & (np.abs(d0) >= max(GRAD_FLOOR[dt], tiny))
     worst = float((np.abs(got[plain] - d0[plain]) / np.abs(d0[plain])).max()) if plain.any() else 0.0
     assert worst <= GRAD_RTOL[dt], \
         f"{what} d_logits: relative error {worst:.3g} on an element without cancellation"
