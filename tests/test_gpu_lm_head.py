@@ -216,8 +216,11 @@ def test_tc_gradients_match_materialised_logits(keep, T):
     z = hr @ wr.t()
     lp0, ent0, _ = kernel_opt.fused_logprob_entropy_scaled(z, t, T)
     dh0, dw0 = torch.autograd.grad((lp0, ent0), (hr, wr), (gl, ge))
-    torch.testing.assert_close(lp.detach(), lp0.detach(), rtol=0, atol=1e-5)
-    torch.testing.assert_close(ent.detach(), ent0.detach(), rtol=1e-4, atol=1e-6)
+    # the reference's logits come from the library GEMM, whose bf16 rounding differs from
+    # the kernel's in rare elements (another summation order): results agree to that
+    # rounding, not bit for bit (exact parity on the kernel's own logits is pinned above)
+    torch.testing.assert_close(lp.detach(), lp0.detach(), rtol=1e-5, atol=1e-4)
+    torch.testing.assert_close(ent.detach(), ent0.detach(), rtol=1e-4, atol=1e-5)
     for a, b in ((dh, dh0), (dw, dw0)):
         scale = float(b.float().abs().max())
         torch.testing.assert_close(a.float(), b.float(), rtol=2e-2, atol=1e-3 * scale)
