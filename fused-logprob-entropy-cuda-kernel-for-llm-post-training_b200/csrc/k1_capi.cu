@@ -707,6 +707,7 @@ int lmh_shape(int64_t n_rows, int64_t hidden, int64_t vocab, int dev, LmhShape* 
     return K1_OK;
 }
 
+// Partials [n_parts][n_rows], target logits [n_rows], the finished-unit counter.
 size_t lmh_workspace_bytes(int64_t n_rows, const LmhShape& sh) {
     return (size_t)sh.n_parts * (size_t)n_rows * sizeof(k1::RowPartial) + (size_t)n_rows * sizeof(float) + 256;
 }
@@ -1127,14 +1128,24 @@ int k1_lm_head_forward(const void* hidden, const void* weight, int64_t n_rows, i
                                     (size_t)sh.n_parts * n_rows * sizeof(k1::RowPartial));
     p.out = reinterpret_cast<__nv_bfloat16*>(logits_out);
     p.out_stride = logits_stride;
+    {
+        // the unit counter after the partials and target logits (16-byte aligned)
+        const size_t off = ((size_t)sh.n_parts * n_rows * sizeof(k1::RowPartial) +
+                            (size_t)n_rows * sizeof(float) + 15) & ~(size_t)15;
+        p.done = reinterpret_cast<unsigned*>(reinterpret_cast<char*>(workspace) + off);
+        cudaError_t e = cudaMemsetAsync(p.done, 0, sizeof(unsigned), s);
+        if (e != cudaSuccess) return fail(K1_ERR_CUDA, "%s: %s", fn, cudaGetErrorString(e));
+    }
     rc = logits_out ? lmh_launch<k1::lmh::STORE>(fn, hidden, weight, n_rows, hidden_dim, vocab,
                                                  scale, p, sh, s)
                     : lmh_launch<k1::lmh::STATS>(fn, hidden, weight, n_rows, hidden_dim, vocab,
                                                  scale, p, sh, s);
     if (rc) return rc;
     const int threads = 256;
+    const unsigned expected =
+        (unsigned)(sh.m_blocks * sh.n_parts) * k1::lmh::EPI_WARPS * (sh.pair ? 2u : 1u);
     k1::lmh::k1_lmhead_merge_kernel<<<(unsigned)((n_rows + threads - 1) / threads), threads, 0, s>>>(
-        p.part, p.xt, targets, n_rows, vocab, sh.n_parts, logprob, entropy, lse);
+        p.part, p.xt, targets, n_rows, vocab, sh.n_parts, p.done, expected, logprob, entropy, lse);
     return check_launch(fn);
 }
 
@@ -1173,9 +1184,9 @@ int k1_lm_head_backward(const void* hidden, const void* weight, int64_t n_rows, 
 #ifdef K1_WAIT_TEST
 // Only in the wait-timeout test library (built with -DK1_WAIT_TEST and short wait limits;
 // not part of libk1_b200.so): sets the knobs that make one block's bounded waits run out
-// on the current device.  withhold: the backward ring's block 0 issues no bulk copy from
-// that chunk on; skip_grab: the one-block-per-SM forward's block 0 drops that grab.  -1
-// turns a knob off.
+// on the current device.  withhold: the backward ring's block 0, and the LM head's CTA 0,
+// issue no bulk copy from that copy number on; skip_grab: the one-block-per-SM forward's
+// block 0 drops that grab.  -1 turns a knob off.
 int k1_test_set_knobs(long long withhold, long long skip_grab) {
     cudaError_t e = cudaMemcpyToSymbol(k1::k1_test_withhold, &withhold, sizeof withhold);
     if (e == cudaSuccess) e = cudaMemcpyToSymbol(k1::k1_test_skip_grab, &skip_grab, sizeof skip_grab);

@@ -98,6 +98,7 @@ struct Params {
     const float* g_lse;
     __nv_bfloat16* out;  // STORE: z; GRAD: dz; [n_rows] rows of out_stride elements
     int64_t out_stride;
+    unsigned* done;      // STATS / STORE: epilogue warps that finished a unit (zeroed per launch)
 };
 
 // ------------------------------------------------------------------------------------
@@ -459,6 +460,12 @@ __global__ void __launch_bounds__(THREADS, 1)
                             ok = false;
                             break;
                         }
+#ifdef K1_WAIT_TEST
+                        if (blockIdx.x == 0 && (long long)issued == k1_test_withhold) {
+                            ok = false;  // test-only: CTA 0 issues nothing more
+                            break;
+                        }
+#endif
                         unsigned char* sa = smem + stage * GE::STAGE_B;
                         const int row_a = x.m_blk * GE::TILE_M + (int)rank * BM;
                         const int row_b = n * BN + (int)rank * GE::LOAD_N;
@@ -542,6 +549,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                             (reinterpret_cast<uintptr_t>(p.out) & 15) == 0;
         int t = 0;
         bool ok = true;
+        int u_fail = -1, n_fail = 0;  // where a wait ran out
         for (int u = me; ok && u < p.units; u += G) {
             const Unit x = unit_of(p, u);
             const int64_t row = (int64_t)x.m_blk * GE::TILE_M + (int64_t)rank * BM + rloc;
@@ -567,6 +575,8 @@ __global__ void __launch_bounds__(THREADS, 1)
                 // warp-uniform: the TMEM loads below are warp-collective
                 if (!__all_sync(0xffffffffu, lmh_wait(&tfull[a], (t >> 1) & 1, abort))) {
                     ok = false;
+                    u_fail = u;
+                    n_fail = n;
                     break;
                 }
                 tc_fence_after();
@@ -634,6 +644,36 @@ __global__ void __launch_bounds__(THREADS, 1)
                     p.part[(int64_t)x.part * p.n_rows + row] = o;
                     if (has_xt) p.xt[row] = xt;
                 }
+                // count this warp's rows of the unit in: the merge kernel turns a launch
+                // with a missing unit (a wait that ran out) into NaN outputs
+                __syncwarp();
+                if (lane == 0) {
+                    __threadfence();
+                    atomicAdd(p.done, 1u);
+                }
+            }
+        }
+        if constexpr (MODE == GRAD) {
+            // a wait ran out: the gradient tiles this thread did not write become NaN
+            if (u_fail >= 0) {
+                const uint32_t nw = DT<__nv_bfloat16>::kNaNWord;
+                uint4 nanv[8];
+#pragma unroll
+                for (int k = 0; k < 8; ++k) nanv[k] = make_uint4(nw, nw, nw, nw);
+                for (int u = u_fail; u < p.units; u += G) {
+                    const Unit x = unit_of(p, u);
+                    const int64_t row = (int64_t)x.m_blk * GE::TILE_M + (int64_t)rank * BM + rloc;
+                    if (row >= p.n_rows) continue;
+                    for (int n = (u == u_fail ? n_fail : x.n0); n < x.n1; ++n) {
+                        for (int c = 0; c < BN / 64; ++c) {
+                            const int64_t col0 = (int64_t)n * BN + c * 64;
+                            const int64_t left = p.vocab - col0;
+                            if (left <= 0) break;
+                            store_chunk(p.out + row * p.out_stride + col0, nanv,
+                                        left < 64 ? (int)left : 64, vec_ok);
+                        }
+                    }
+                }
             }
         }
     }
@@ -658,11 +698,18 @@ __global__ void __launch_bounds__(THREADS, 1)
 }
 
 // Merge the units' partials of every row (fp64, in part order) and finish the row.
+// A launch that did not finish every unit (a bounded wait ran out) gives NaN for all rows.
 __global__ void k1_lmhead_merge_kernel(const RowPartial* part, const float* xt,
                                        const int64_t* targets, int64_t n_rows, int64_t vocab,
-                                       int n_parts, float* logprob, float* entropy, float* lse) {
+                                       int n_parts, const unsigned* done, unsigned expected,
+                                       float* logprob, float* entropy, float* lse) {
     const int64_t row = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (row >= n_rows) return;
+    if (*done != expected) {
+        const float nan = __int_as_float(0x7fc00000);
+        logprob[row] = entropy[row] = lse[row] = nan;
+        return;
+    }
     RowPartial acc;
     acc.m = -INFINITY;
     acc.z = acc.t = 0.0;

@@ -8,7 +8,8 @@ short wait limits) and its knobs to make one block's waits run out on purpose:
   * backward: block 0's producer issues no bulk copy from chunk 3 on, so its consumers'
     waits for chunk 3 run out;
   * forward: block 0 drops one grab of row 0, so row 0 never completes and the grabs of
-    the next row that needs its slot wait until their waits run out.
+    the next row that needs its slot wait until their waits run out;
+  * tensor-core LM head: CTA 0 stops issuing tile copies, so its MMA's wait runs out.
 
 Nothing faults or hangs: the waits give up after a few milliseconds, the producer drains
 the copies it issued, and the kernel returns.  Each test checks the status bit through
@@ -20,7 +21,7 @@ import ctypes
 import pytest
 import torch
 
-from _helpers import WAIT_TEST_LIB
+from _helpers import CAPI_LIB, WAIT_TEST_LIB
 from kernel_opt import _C
 
 pytestmark = pytest.mark.gpu
@@ -167,3 +168,76 @@ def test_check_waits_switch_is_quiet_when_nothing_runs_out():
         assert torch.isfinite(d).all()
     finally:
         kernel_opt.set_check_waits(was)
+
+
+def _lmh_api(lib):
+    i64, p, f32 = ctypes.c_int64, ctypes.c_void_p, ctypes.c_float
+    lib.k1_lm_head_workspace_bytes.argtypes = [i64, i64, i64, ctypes.c_int]
+    lib.k1_lm_head_workspace_bytes.restype = ctypes.c_size_t
+    lib.k1_lm_head_forward.argtypes = [p, p, i64, i64, i64, f32, p, p, p, p, p, i64, p,
+                                       ctypes.c_size_t, p]
+    lib.k1_lm_head_backward.argtypes = [p, p, i64, i64, i64, f32, p, p, p, p, p, p, p, i64, p]
+    return lib
+
+
+def _lmh_run(lib, h, w, t, scale, lse=None, ent=None, gl=None):
+    N, H = h.shape
+    V = w.shape[0]
+    s = torch.cuda.current_stream().cuda_stream
+    if lse is None:
+        ws = torch.empty(lib.k1_lm_head_workspace_bytes(N, H, V, 0), dtype=torch.uint8,
+                         device="cuda")
+        out = [torch.full((N,), 7.0, device="cuda") for _ in range(3)]
+        rc = lib.k1_lm_head_forward(h.data_ptr(), w.data_ptr(), N, H, V, scale, t.data_ptr(),
+                                    *(o.data_ptr() for o in out), None, V, ws.data_ptr(),
+                                    ws.numel(), s)
+        assert rc == 0, lib.k1_last_error()
+        torch.cuda.synchronize()
+        return out
+    d = torch.full((N, V), 7.0, dtype=torch.bfloat16, device="cuda")
+    rc = lib.k1_lm_head_backward(h.data_ptr(), w.data_ptr(), N, H, V, scale, t.data_ptr(),
+                                 lse.data_ptr(), ent.data_ptr(), gl.data_ptr(), None, None,
+                                 d.data_ptr(), V, s)
+    assert rc == 0, lib.k1_last_error()
+    torch.cuda.synchronize()
+    return d
+
+
+def test_lm_head_wait_runs_out():
+    """The tensor-core LM head: CTA 0 issues no tile copy from its 5th on, so its MMA's wait
+    for that stage runs out; the kernel returns, sets bit 3, the forward's statistics become
+    NaN (a unit is missing, so every row is) and the gradient's unfinished tiles NaN."""
+    lib = _lmh_api(test_lib())
+    prod = _lmh_api(ctypes.CDLL(CAPI_LIB))
+    g = torch.Generator(device="cuda").manual_seed(21)
+    N, H, V = 512, 256, 4096
+    h = (torch.randn(N, H, generator=g, device="cuda") * 0.5).to(torch.bfloat16)
+    w = (torch.randn(V, H, generator=g, device="cuda") * 0.15).to(torch.bfloat16)
+    t = torch.randint(0, V, (N,), generator=g, device="cuda")
+    gl = torch.full((N,), -1.0 / N, device="cuda")
+    ref = _lmh_run(prod, h, w, t, 1.0)
+    dref = _lmh_run(prod, h, w, t, 1.0, ref[2], ref[1], gl)
+    assert status(lib) == 0
+
+    assert lib.k1_test_set_knobs(5, -1) == 0
+    try:
+        out = _lmh_run(lib, h, w, t, 1.0)
+        st_f = status(lib)
+        d = _lmh_run(lib, h, w, t, 1.0, ref[2], ref[1], gl)
+        st_b = status(lib)
+    finally:
+        assert lib.k1_test_set_knobs(-1, -1) == 0
+    assert st_f & 8 and st_b & 8, f"status {st_f}, {st_b}: the LM head's wait did not report"
+    for o in out:
+        assert torch.isnan(o).all()
+    bad = torch.isnan(d.float())
+    assert bad.any()
+    assert torch.equal(d[~bad], dref[~bad])
+
+    # the same context, knob off: clean and identical to the product library
+    out2 = _lmh_run(lib, h, w, t, 1.0)
+    d2 = _lmh_run(lib, h, w, t, 1.0, ref[2], ref[1], gl)
+    assert status(lib) == 0
+    for a, b in zip(out2, ref):
+        assert torch.equal(a, b)
+    assert torch.equal(d2, dref)
