@@ -695,7 +695,8 @@ int lmh_shape(int64_t n_rows, int64_t hidden, int64_t vocab, int dev, LmhShape* 
     const int tile_m = k1::lmh::BM * (sh->pair ? 2 : 1);
     sh->m_blocks = (int)((n_rows + tile_m - 1) / tile_m);
     sh->n_tiles = (int)((vocab + k1::lmh::BN - 1) / k1::lmh::BN);
-    sh->k_blocks = (int)((hidden + k1::lmh::BK - 1) / k1::lmh::BK);
+    const int kb = sh->pair ? k1::lmh::Geo<true>::KB : k1::lmh::Geo<false>::KB;  // K per stage
+    sh->k_blocks = (int)((hidden + kb - 1) / kb);
     const int64_t max_units = (int64_t)sh->m_blocks * sh->n_tiles;
     int slots = sms;
     if (sh->pair) {

@@ -81,7 +81,7 @@ enum Mode : int { STATS = 0, STORE = 1, GRAD = 2 };
 
 struct Params {
     int64_t n_rows, vocab;
-    int k_blocks;     // ceil(hidden / BK); copies beyond `hidden` read zeros
+    int k_blocks;     // ceil(hidden / K per stage); copies beyond `hidden` read zeros
     int m_blocks;     // ceil(n_rows / BM)
     int n_tiles;      // ceil(vocab / BN)
     int n_parts;      // units per row block
@@ -307,17 +307,25 @@ __device__ __forceinline__ void store_chunk(__nv_bfloat16* dst, const uint4 (&v)
 // CTA holds its 128 rows of h and its 128 rows of W per K block (32 KB; 6 stages), its
 // own 128 x 256 half of the accumulator in its own TMEM, and runs its own epilogue.  The
 // pair moves half the bytes per flop through shared memory and L2 of the single CTA.
+#ifndef K1_LMH_PAIR_KSUB
+#define K1_LMH_PAIR_KSUB 2  // 64-wide K sub-blocks per pair stage: 1 or 2
+#endif
+#ifndef K1_LMH_PAIR_STAGES
+#define K1_LMH_PAIR_STAGES (K1_LMH_PAIR_KSUB == 2 ? 3 : 6)
+#endif
+static_assert(K1_LMH_PAIR_KSUB == 1 || K1_LMH_PAIR_KSUB == 2, "1 or 2 K sub-blocks per stage");
 template <bool PAIR>
 struct Geo {
     static constexpr int CTAS = PAIR ? 2 : 1;
     static constexpr int TILE_M = BM * CTAS;        // rows per tile (all CTAs of the pair)
     static constexpr int LOAD_N = BN / CTAS;        // W rows per CTA and K block
-    static constexpr int A_B = BM * BK * 2;         // 16 KB
-    static constexpr int B_B = LOAD_N * BK * 2;     // 32 KB alone, 16 KB in a pair
+    static constexpr int KSUB = PAIR ? K1_LMH_PAIR_KSUB : 1;  // 64-wide K sub-blocks per stage
+    static constexpr int KB = BK * KSUB;            // K per stage
+    static constexpr int A_SUB = BM * BK * 2;       // 16 KB: one swizzled 128 x 64 box of h
+    static constexpr int B_SUB = LOAD_N * BK * 2;   // 32 KB alone, 16 KB in a pair
+    static constexpr int A_B = KSUB * A_SUB;
+    static constexpr int B_B = KSUB * B_SUB;
     static constexpr int STAGE_B = A_B + B_B;
-#ifndef K1_LMH_PAIR_STAGES
-#define K1_LMH_PAIR_STAGES 6
-#endif
     static constexpr int NSTAGE = PAIR ? K1_LMH_PAIR_STAGES : STAGES;
     static constexpr int SMEM = 1024 + NSTAGE * STAGE_B + 256;
     static constexpr uint32_t IDESC = (1u << 4) | (1u << 7) | (1u << 10) |
@@ -471,8 +479,13 @@ __global__ void __launch_bounds__(THREADS, 1)
                         const int row_b = n * BN + (int)rank * GE::LOAD_N;
                         if constexpr (PAIR) {
                             const uint32_t cl = mapa(ring::saddr(&full[stage]), 0);
-                            tma_load_2d_pair(sa, &tmap_h, kb * BK, row_a, cl);
-                            tma_load_2d_pair(sa + GE::A_B, &tmap_w, kb * BK, row_b, cl);
+#pragma unroll
+                            for (int j = 0; j < GE::KSUB; ++j)
+                                tma_load_2d_pair(sa + j * GE::A_SUB, &tmap_h, kb * GE::KB + j * BK, row_a, cl);
+#pragma unroll
+                            for (int j = 0; j < GE::KSUB; ++j)
+                                tma_load_2d_pair(sa + GE::A_B + j * GE::B_SUB, &tmap_w, kb * GE::KB + j * BK,
+                                                 row_b, cl);
                             if (leader)
                                 ring::arrive_expect(&full[stage], GE::CTAS * GE::STAGE_B);
                             else
@@ -484,7 +497,8 @@ __global__ void __launch_bounds__(THREADS, 1)
                         }
                         // the next tile's W rows of this K block into L2, a tile ahead
                         if (K1_LMH_PREFETCH && n + 1 < x.n1)
-                            tma_prefetch_l2(&tmap_w, kb * BK, row_b + BN);
+                            for (int j = 0; j < GE::KSUB; ++j)
+                                tma_prefetch_l2(&tmap_w, kb * GE::KB + j * BK, row_b + BN);
                         ++issued;
                         if (++stage == NST) {
                             stage = 0;
@@ -523,10 +537,14 @@ __global__ void __launch_bounds__(THREADS, 1)
                         }
                         tc_fence_after();
                         const uint32_t sa = sbase + stage * GE::STAGE_B;
-                        const uint64_t da = smem_desc(sa), db = smem_desc(sa + GE::A_B);
 #pragma unroll
-                        for (int k = 0; k < BK / UK; ++k)  // +32 bytes per K slice: +2 in >> 4 units
-                            umma_t<PAIR>(d, da + 2 * k, db + 2 * k, (kb > 0 || k > 0) ? 1u : 0u);
+                        for (int j = 0; j < GE::KSUB; ++j) {
+                            const uint64_t da = smem_desc(sa + j * GE::A_SUB);
+                            const uint64_t db = smem_desc(sa + GE::A_B + j * GE::B_SUB);
+#pragma unroll
+                            for (int k = 0; k < BK / UK; ++k)  // +32 bytes per K slice: +2 in >> 4 units
+                                umma_t<PAIR>(d, da + 2 * k, db + 2 * k, (kb > 0 || j > 0 || k > 0) ? 1u : 0u);
+                        }
                         commit_t<PAIR>(&empty[stage]);  // the stage is free once these MMAs ran
                         if (++stage == NST) {
                             stage = 0;
