@@ -168,7 +168,7 @@ class ClockSampler:
     }
 
     def __init__(self, device, period_s: float = 0.002):
-        self.samples, self.reasons, self.ok = [], 0, False
+        self.samples, self.power, self.reasons, self.ok = [], [], 0, False
         self.period = period_s
         self._stop = threading.Event()
         try:
@@ -195,6 +195,7 @@ class ClockSampler:
             try:
                 self.samples.append(nv.nvmlDeviceGetClockInfo(self.h, nv.NVML_CLOCK_SM))
                 self.reasons |= self._reasons_fn(self.h)
+                self.power.append(nv.nvmlDeviceGetPowerUsage(self.h) / 1000.0)
             except Exception:
                 pass
             time.sleep(self.period)
@@ -215,8 +216,11 @@ class ClockSampler:
             return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": ["unavailable"],
                     "samples": 0}
         names = [k for k, bit in self.REASONS.items() if self.reasons & bit]
-        return {"sm_mhz": statistics.median(self.samples), "sm_max_mhz": self.max_mhz,
-                "reasons": names, "samples": len(self.samples)}
+        out = {"sm_mhz": statistics.median(self.samples), "sm_max_mhz": self.max_mhz,
+               "reasons": names, "samples": len(self.samples)}
+        if self.power:
+            out["power_w"] = round(statistics.median(self.power), 1)
+        return out
 
 
 # ---------------------------------------------------------------------------------------
@@ -1214,6 +1218,27 @@ def lmhead_arm(args, cfg, rank, local_rank, world):
             "fused_forward_kernel_ms": timed(kernel_only, False, K),
             "library_gemm_ms": timed(library_gemm, False, K),
         }
+    def sustained(fn, seconds):
+        # back to back for `seconds`, long enough to reach the board's power cap: TFLOP/s
+        # with the median SM clock and board power seen meanwhile
+        reps = max(5, int(seconds * 1e3 / timed(fn, False, 3)))
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with ClockSampler(device, period_s=0.02) as cs:
+            a.record(stream)
+            for _ in range(reps):
+                fn(False)
+            b.record(stream)
+            torch.cuda.synchronize(device)
+        c = cs.summary()
+        ms = a.elapsed_time(b) / reps
+        return {"tflops": round(gemm_flops / (ms / 1e3) / 1e12, 1), "ms": round(ms, 3), "reps": reps,
+                "sm_mhz": c["sm_mhz"], "power_w": c.get("power_w"), "reasons": c["reasons"]}
+
+    sus = {}
+    if args.lmh_sustained > 0:
+        for _ in range(2):  # interleaved, so both see the same thermal history
+            for name, fn in (("fused_forward_kernel", kernel_only), ("library_gemm", library_gemm)):
+                sus.setdefault(name, []).append(sustained(fn, args.lmh_sustained))
     del zbuf
     torch.cuda.empty_cache()
     mem = {"fused_train": peak_extra(fused_step, True),
@@ -1263,6 +1288,9 @@ def lmhead_arm(args, cfg, rank, local_rank, world):
         "gpu_launches": 2 * K,
         "clocks": clocks.summary(),
     }
+    if sus:
+        out["sustained"] = dict(sus, note=f"each kernel back to back for ~{args.lmh_sustained:g} s "
+                                          "(at the power cap), the two interleaved, 2 rounds")
     print(json.dumps(out), flush=True)
 
 
@@ -1357,6 +1385,9 @@ def main():
                     help="skip the config 5 vocab-parallel sub-record")
     ap.add_argument("--lmh-rows", type=int, default=0,
                     help="--mode lmhead: rows (default 16384; smaller for profiling)")
+    ap.add_argument("--lmh-sustained", type=float, default=2.0,
+                    help="--mode lmhead: seconds per sustained (power-capped) run of the fused "
+                         "forward kernel and of the library GEMM; 0 skips them")
     ap.add_argument("--lmh-vocab", type=int, default=0,
                     help="--mode lmhead: vocabulary (default 151936; smaller for profiling)")
     ap.add_argument("--eager", action="store_true",

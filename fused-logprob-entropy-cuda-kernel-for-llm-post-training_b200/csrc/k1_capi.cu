@@ -606,12 +606,13 @@ int make_tmap(CUtensorMap* m, const void* base, int64_t rows, int64_t cols, int 
 }
 
 // Units per row block: the number of runs the vocabulary tiles are cut into.  Chosen among
-// runs of 4 to 32 tiles so that the CTA with the most tiles (units are dealt round robin,
-// in the kernel's unit order) has as few as possible; cached per shape.
-int lmh_parts(int m_blocks, int n_tiles, int grid) {
+// runs of 1 to 32 tiles (the per-row partials kept within 64 MiB) so that the CTA with the
+// most tiles (units are dealt round robin, in the kernel's unit order) has as few as
+// possible, the fewest parts among equals; cached per shape.
+int lmh_parts(int m_blocks, int tile_m, int n_tiles, int grid) {
     static std::mutex mu;
-    static std::map<std::tuple<int, int, int>, int> cache;
-    const auto key = std::make_tuple(m_blocks, n_tiles, grid);
+    static std::map<std::tuple<int, int, int, int>, int> cache;
+    const auto key = std::make_tuple(m_blocks, tile_m, n_tiles, grid);
     {
         std::lock_guard<std::mutex> lock(mu);
         auto it = cache.find(key);
@@ -619,7 +620,10 @@ int lmh_parts(int m_blocks, int n_tiles, int grid) {
     }
     int best = 1;
     int64_t best_max = INT64_MAX;
-    const int lo = std::max(1, (n_tiles + 31) / 32), hi = std::max(lo, (n_tiles + 3) / 4);
+    const int64_t rows = (int64_t)m_blocks * tile_m;
+    const int64_t cap = ((int64_t)64 << 20) / (rows * (int64_t)sizeof(k1::RowPartial));
+    const int lo = std::max(1, (n_tiles + 31) / 32);
+    const int hi = (int)std::max<int64_t>(lo, std::min<int64_t>(std::min(n_tiles, 2048), cap));
     std::vector<int64_t> load(grid);
     for (int np = lo; np <= hi; ++np) {
         std::fill(load.begin(), load.end(), 0);
@@ -704,7 +708,7 @@ int lmh_shape(int64_t n_rows, int64_t hidden, int64_t vocab, int dev, LmhShape* 
         if (rc) return rc;
     }
     sh->grid = (int)std::min<int64_t>(slots, max_units);
-    sh->n_parts = lmh_parts(sh->m_blocks, sh->n_tiles, sh->grid);
+    sh->n_parts = lmh_parts(sh->m_blocks, tile_m, sh->n_tiles, sh->grid);
     return K1_OK;
 }
 

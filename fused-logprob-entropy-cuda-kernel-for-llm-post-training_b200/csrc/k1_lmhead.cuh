@@ -19,15 +19,19 @@
 // K block and its 128 x 256 half of the accumulator; the single-CTA variant (K1_LMH_PAIR=0)
 // computes 128 x 256 tiles alone.
 //   warp 0   TMA producer: 2-D tiled bulk-tensor copies (128-byte swizzle; every copy
-//            reads this GPU's own memory into this CTA's own shared memory) of 64-wide
-//            K blocks of h and W into a ring (pair: 6 stages of 32 KB; single: 4 of
-//            48 KB), completion counted on the pair leader's mbarrier;
-//   warp 1   MMA issuer (the pair's first CTA): per K block, four tcgen05.mma of kind::f16
-//            (bf16 x bf16 -> fp32, K = 16 each) from shared memory into one of two
-//            256-column TMEM accumulators; tcgen05.commit releases the stage in both CTAs
-//            and, after the last K block, hands the accumulator to both epilogues;
+//            reads this GPU's own memory into this CTA's own shared memory) of K blocks
+//            of h and W into a ring (pair: 3 stages of 64 KB, each two 64-wide K
+//            sub-blocks; single: 4 stages of 48 KB, one 64-wide K block), completion
+//            counted on the pair leader's mbarrier;
+//   warp 1   MMA issuer (the pair's first CTA): per 64-wide K sub-block, four tcgen05.mma
+//            of kind::f16 (bf16 x bf16 -> fp32, K = 16 each) from shared memory into one
+//            of two 256-column TMEM accumulators; tcgen05.commit releases the stage in
+//            both CTAs and, after the last K block, hands the accumulator to both
+//            epilogues.  A pair stage carries 1024 cycles of tensor work, twice the cost
+//            of the stage's handshake (empty -> copies -> full -> MMAs -> commit), so the
+//            handshakes stay off the tensor pipe's critical path;
 //   warps 2-5  epilogue: each thread owns one row of its CTA's half tile (TMEM lane = row)
-//            and reads its 256 fp32 accumulators 64 columns per wait with tcgen05.ld
+//            and reads its 256 fp32 accumulators 32 columns per wait with tcgen05.ld
 //            (32x32b.x32), while the tensor cores fill the other accumulator.
 // Work is cut into units of (a tile's rows, a run of consecutive 256-column tiles); the
 // epilogue keeps each row's K1 state in registers across the unit's tiles and writes one
@@ -60,7 +64,7 @@ constexpr int TMEM_COLS = NUM_ACC * BN;  // 512: all of TMEM, so one CTA per SM
 constexpr int EPI_WARPS = 4;
 constexpr int THREADS = (2 + EPI_WARPS) * 32;
 #ifndef K1_LMH_CW
-#define K1_LMH_CW 64  // epilogue columns per TMEM wait: 32 or 64
+#define K1_LMH_CW 32  // epilogue columns per TMEM wait: 32 or 64
 #endif
 static_assert(K1_LMH_CW == 32 || K1_LMH_CW == 64, "32 or 64 columns per epilogue step");
 #ifndef K1_LMH_PREFETCH
@@ -250,16 +254,20 @@ __device__ __forceinline__ void pack_tile_chunk(const uint32_t (&r)[CW], int val
         v[u] = make_uint4(w[4 * u], w[4 * u + 1], w[4 * u + 2], w[4 * u + 3]);
 }
 
-// Element k (0..CW-1) of a packed chunk as fp32 (k known at run time: unrolled selects).
+// Element k (0..CW-1) of a packed chunk as fp32.  k is known only at run time: one
+// compare-and-select per word, every register named statically, so the chunk never goes
+// through local memory (whose L1 traffic would compete with the tensor cores' operand
+// reads from shared memory).
 template <int NV>
 __device__ __forceinline__ float chunk_elem(const uint4 (&v)[NV], int k) {
+    const int j = k >> 1;
     uint32_t w = 0;
 #pragma unroll
     for (int u = 0; u < NV; ++u) {
-        if ((k >> 3) == u) {
-            const int i = (k >> 1) & 3;
-            w = i == 0 ? v[u].x : i == 1 ? v[u].y : i == 2 ? v[u].z : v[u].w;
-        }
+        w = j == 4 * u + 0 ? v[u].x : w;
+        w = j == 4 * u + 1 ? v[u].y : w;
+        w = j == 4 * u + 2 ? v[u].z : w;
+        w = j == 4 * u + 3 ? v[u].w : w;
     }
     return (k & 1) ? __uint_as_float(w & 0xFFFF0000u) : __uint_as_float(w << 16);
 }
@@ -287,7 +295,25 @@ __device__ __forceinline__ void scale_chunk(uint4 (&v)[NV], int valid, float s) 
     }
 }
 
-// Store the first `valid` bf16 columns of a packed chunk of one row.
+// Element k (0..CW-1) of a packed chunk replaced by bf16(val), with the same statically
+// named selects as chunk_elem.
+template <int NV>
+__device__ __forceinline__ void set_chunk_elem(uint4 (&v)[NV], int k, float val) {
+    const int j = k >> 1;
+    const uint32_t b = (uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(val));
+    const uint32_t keep = (k & 1) ? 0x0000FFFFu : 0xFFFF0000u;
+    const uint32_t put = (k & 1) ? (b << 16) : b;
+#pragma unroll
+    for (int u = 0; u < NV; ++u) {
+        v[u].x = j == 4 * u + 0 ? ((v[u].x & keep) | put) : v[u].x;
+        v[u].y = j == 4 * u + 1 ? ((v[u].y & keep) | put) : v[u].y;
+        v[u].z = j == 4 * u + 2 ? ((v[u].z & keep) | put) : v[u].z;
+        v[u].w = j == 4 * u + 3 ? ((v[u].w & keep) | put) : v[u].w;
+    }
+}
+
+// Store the first `valid` bf16 columns of a packed chunk of one row (the ragged or
+// unaligned case element by element, every register named statically).
 template <int NV>
 __device__ __forceinline__ void store_chunk(__nv_bfloat16* dst, const uint4 (&v)[NV], int valid,
                                             bool vec_ok) {
@@ -296,7 +322,17 @@ __device__ __forceinline__ void store_chunk(__nv_bfloat16* dst, const uint4 (&v)
 #pragma unroll
         for (int u = 0; u < NV; ++u) stg_stream(d + u, v[u]);
     } else {
-        for (int k = 0; k < NV * 8 && k < valid; ++k) dst[k] = __float2bfloat16_rn(chunk_elem(v, k));
+        unsigned short* d = reinterpret_cast<unsigned short*>(dst);
+#pragma unroll
+        for (int u = 0; u < NV; ++u) {
+            const uint32_t w[4] = {v[u].x, v[u].y, v[u].z, v[u].w};
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const int c = u * 8 + 2 * i;
+                if (c < valid) d[c] = (unsigned short)(w[i] & 0xFFFFu);
+                if (c + 1 < valid) d[c + 1] = (unsigned short)(w[i] >> 16);
+            }
+        }
     }
 }
 
@@ -623,9 +659,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                             if (SCALED) y = scale1<__nv_bfloat16>(y, p.scale);
                             const float g = scale1<__nv_bfloat16>(
                                 DT<__nv_bfloat16>::round1(bwd_target_value(y, q)), p.scale);
-#pragma unroll
-                            for (int u = 0; u < CW / 8; ++u)
-                                if ((k >> 3) == u) o[u] = vec_set<__nv_bfloat16>(o[u], k & 7, g);
+                            set_chunk_elem(o, k, g);
                         }
                         if (live) store_chunk(dst, o, valid, vec_ok);
                     } else {

@@ -204,9 +204,10 @@ def _lmh_run(lib, h, w, t, scale, lse=None, ent=None, gl=None):
 
 
 def test_lm_head_wait_runs_out():
-    """The tensor-core LM head: CTA 0 issues no tile copy from its 5th on, so its MMA's wait
-    for that stage runs out; the kernel returns, sets bit 3, the forward's statistics become
-    NaN (a unit is missing, so every row is) and the gradient's unfinished tiles NaN."""
+    """The tensor-core LM head: CTA 0 issues no tile copy from its 2nd stage on (every tile
+    here takes two stages: H = 256 in K blocks of 128), so its MMA's wait for that stage
+    runs out; the kernel returns, sets bit 3, the forward's statistics become NaN (a unit
+    is missing, so every row is) and the gradient's unfinished tiles NaN."""
     lib = _lmh_api(test_lib())
     prod = _lmh_api(ctypes.CDLL(CAPI_LIB))
     g = torch.Generator(device="cuda").manual_seed(21)
@@ -219,7 +220,7 @@ def test_lm_head_wait_runs_out():
     dref = _lmh_run(prod, h, w, t, 1.0, ref[2], ref[1], gl)
     assert status(lib) == 0
 
-    assert lib.k1_test_set_knobs(5, -1) == 0
+    assert lib.k1_test_set_knobs(1, -1) == 0
     try:
         out = _lmh_run(lib, h, w, t, 1.0)
         st_f = status(lib)
