@@ -314,10 +314,22 @@ __device__ __forceinline__ void set_chunk_elem(uint4 (&v)[NV], int k, float val)
 
 // Store the first `valid` bf16 columns of a packed chunk of one row (the ragged or
 // unaligned case element by element, every register named statically).
+// 32 bytes at a 32-byte aligned address in one store.
+__device__ __forceinline__ void stg32(void* p, uint4 a, uint4 b) {
+    asm volatile("st.global.v8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"l"(p), "r"(a.x),
+                 "r"(a.y), "r"(a.z), "r"(a.w), "r"(b.x), "r"(b.y), "r"(b.z), "r"(b.w)
+                 : "memory");
+}
+
+// vec: 16-byte aligned row pieces (16-byte stores); vec32: 32-byte aligned (32-byte stores,
+// half the store instructions, each touching the warp's 32 rows once).
 template <int NV>
 __device__ __forceinline__ void store_chunk(__nv_bfloat16* dst, const uint4 (&v)[NV], int valid,
-                                            bool vec_ok) {
-    if (vec_ok && valid >= NV * 8) {
+                                            bool vec_ok, bool vec32_ok = false) {
+    if (vec32_ok && valid >= NV * 8 && NV % 2 == 0) {
+#pragma unroll
+        for (int u = 0; u < NV; u += 2) stg32(reinterpret_cast<uint4*>(dst) + u, v[u], v[u + 1]);
+    } else if (vec_ok && valid >= NV * 8) {
         uint4* d = reinterpret_cast<uint4*>(dst);
 #pragma unroll
         for (int u = 0; u < NV; ++u) stg_stream(d + u, v[u]);
@@ -601,6 +613,8 @@ __global__ void __launch_bounds__(THREADS, 1)
         const uint32_t tlane = tmem + ((uint32_t)(quarter * 32) << 16);
         const bool vec_ok = (p.out_stride & 7) == 0 &&
                             (reinterpret_cast<uintptr_t>(p.out) & 15) == 0;
+        const bool vec32_ok = (p.out_stride & 15) == 0 &&
+                              (reinterpret_cast<uintptr_t>(p.out) & 31) == 0;
         int t = 0;
         bool ok = true;
         int u_fail = -1, n_fail = 0;  // where a wait ran out
@@ -661,10 +675,10 @@ __global__ void __launch_bounds__(THREADS, 1)
                                 DT<__nv_bfloat16>::round1(bwd_target_value(y, q)), p.scale);
                             set_chunk_elem(o, k, g);
                         }
-                        if (live) store_chunk(dst, o, valid, vec_ok);
+                        if (live) store_chunk(dst, o, valid, vec_ok, vec32_ok);
                     } else {
                         if constexpr (MODE == STORE) {
-                            if (live) store_chunk(dst, v, valid, vec_ok);
+                            if (live) store_chunk(dst, v, valid, vec_ok, vec32_ok);
                         }
                         if constexpr (SCALED) scale_chunk(v, valid, p.scale);
                         if (tcol >= col0 && tcol < col0 + CW) {
