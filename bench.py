@@ -1123,7 +1123,9 @@ def lmhead_arm(args, cfg, rank, local_rank, world):
                       autograd (3 GEMMs).
     Training step (forward + backward to hidden and weight) and no-grad forward (the
     old-policy / reference-policy log-probs of GRPO), peak extra device memory of each, and
-    the fused forward kernel's own TFLOP/s against the library GEMM of the same shape."""
+    the fused forward kernel's own TFLOP/s against the library GEMM of the same shape.  The
+    arms compared with each other take turns step by step (per-step events, medians), so
+    they share the power-cap and thermal history."""
     import torch.distributed as dist
 
     import kernel_opt
@@ -1204,20 +1206,37 @@ def lmhead_arm(args, cfg, rank, local_rank, world):
     def library_gemm(_grad):
         torch.mm(h, w.t(), out=zbuf)
 
+    def interleaved(arms, grad, K):
+        # the arms take turns step by step (each step timed alone, median over K), so all
+        # of them run under the same power-cap and thermal history
+        for fn in arms.values():
+            for _ in range(max(3, args.warmup)):
+                with torch.set_grad_enabled(grad):
+                    fn(grad)
+        torch.cuda.synchronize(device)
+        got = {k: [] for k in arms}
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        for _ in range(K):
+            for k, fn in arms.items():
+                a.record(stream)
+                with torch.set_grad_enabled(grad):
+                    fn(grad)
+                b.record(stream)
+                torch.cuda.synchronize(device)
+                got[k].append(a.elapsed_time(b))
+        return {k: statistics.median(v) for k, v in got.items()}
+
     K = max(1, min(args.steps, 10))
     with ClockSampler(device) as clocks:
         if world > 1:
             dist.barrier(device_ids=[local_rank])
-        fused_ms = timed(fused_step, True, K)
-        res = {
-            "fused_train_ms": fused_ms,
-            "fused_keep_train_ms": timed(fused_keep_step, True, K),
-            "materialised_train_ms": timed(materialised_step, True, K),
-            "fused_nograd_ms": timed(fused_step, False, K),
-            "materialised_nograd_ms": timed(materialised_step, False, K),
-            "fused_forward_kernel_ms": timed(kernel_only, False, K),
-            "library_gemm_ms": timed(library_gemm, False, K),
-        }
+        res = {}
+        res.update(interleaved({"fused_train_ms": fused_step, "fused_keep_train_ms": fused_keep_step,
+                                "materialised_train_ms": materialised_step}, True, K))
+        res.update(interleaved({"fused_nograd_ms": fused_step,
+                                "materialised_nograd_ms": materialised_step}, False, K))
+        res.update(interleaved({"fused_forward_kernel_ms": kernel_only,
+                                "library_gemm_ms": library_gemm}, False, K))
     def sustained(fn, seconds):
         # back to back for `seconds`, long enough to reach the board's power cap: TFLOP/s
         # with the median SM clock and board power seen meanwhile
