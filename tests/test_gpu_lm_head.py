@@ -131,8 +131,12 @@ def test_leading_dims_and_default_chunk():
 # ---------------------------------------------------------------------------------------
 # bf16: the tensor-core kernel
 # ---------------------------------------------------------------------------------------
+# H = 136 and 64: the last pipeline stage's second 64-wide K box lies wholly beyond H
+# (read as zeros by the tensor copy).  Row stores: V = 32768 and 2064 take 32-byte stores
+# (2064: a 16-column tail stored element by element), 1000, 3000 and 1544 16-byte
+# stores, 777 and 4099 element by element.
 TC_SHAPES = [(300, 256, 1000), (257, 200, 777), (640, 512, 3000), (129, 3584, 4099),
-             (1024, 1024, 32768)]
+             (1024, 1024, 32768), (200, 136, 1544), (1000, 64, 2064)]
 
 
 def _tc_problem(N, H, V, seed):
@@ -186,7 +190,7 @@ def test_tc_statistics_match_k1_and_oracle(shape, T):
     assert torch.equal(lp2, lp) and torch.equal(ent2, ent) and torch.equal(lse2, lse)
 
 
-@pytest.mark.parametrize("shape", TC_SHAPES[:4])
+@pytest.mark.parametrize("shape", TC_SHAPES[:4] + TC_SHAPES[5:])
 @pytest.mark.parametrize("T", [1.0, 0.7])
 def test_tc_recomputed_gradient_is_k1_backward(shape, T):
     h, w, t = _tc_problem(*shape, seed=12)
