@@ -786,6 +786,103 @@ int lmh_launch(const char* fn, const void* hidden, const void* weight, int64_t n
     if (rc) return rc;
     return check_launch(fn);
 }
+// The LM head's forward: the tensor-core kernel (statistics, or statistics + z), then the
+// merge of the per-unit partials into either the finished rows (logprob, entropy, lse) or,
+// for a vocabulary shard, each row's k1_partial.  col_offset: the global id of the weight's
+// first row (0 for a whole vocabulary).
+int lmh_forward(const char* fn, const void* hidden, const void* weight, int64_t n_rows,
+                int64_t hidden_dim, int64_t vocab, int64_t col_offset, float scale,
+                const int64_t* targets, float* logprob, float* entropy, float* lse,
+                k1_partial* partials, void* logits_out, int64_t logits_stride, void* workspace,
+                size_t workspace_bytes, void* stream) {
+    int rc = lmh_check(fn, hidden, weight, n_rows, hidden_dim, vocab);
+    if (rc) return rc;
+    if (n_rows == 0) return K1_OK;
+    if (!targets) return fail(K1_ERR_INVALID_ARGUMENT, "%s: NULL targets or output pointer", fn);
+    if (!(scale > 0.f) || !std::isfinite(scale))
+        return fail(K1_ERR_INVALID_ARGUMENT, "%s: scale must be positive and finite", fn);
+    if (logits_out && logits_stride < vocab)
+        return fail(K1_ERR_INVALID_ARGUMENT, "%s: logits_stride must be >= vocab", fn);
+    int dev = 0;
+    rc = current_device(&dev);
+    if (rc) return rc;
+    LmhShape sh;
+    rc = lmh_shape(n_rows, hidden_dim, vocab, dev, &sh);
+    if (rc) return rc;
+    const size_t need = lmh_workspace_bytes(n_rows, sh);
+    if (!workspace || workspace_bytes < need)
+        return fail(K1_ERR_WORKSPACE, "%s: workspace of %zu bytes required (got %zu)", fn, need,
+                    workspace ? workspace_bytes : (size_t)0);
+    if (reinterpret_cast<uintptr_t>(workspace) % 16 != 0)
+        return fail(K1_ERR_INVALID_ARGUMENT, "%s: workspace must be 16-byte aligned", fn);
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    k1::lmh::Params p = {};
+    p.col_offset = col_offset;
+    p.targets = targets;
+    p.part = reinterpret_cast<k1::RowPartial*>(workspace);
+    p.xt = reinterpret_cast<float*>(reinterpret_cast<char*>(workspace) +
+                                    (size_t)sh.n_parts * n_rows * sizeof(k1::RowPartial));
+    p.out = reinterpret_cast<__nv_bfloat16*>(logits_out);
+    p.out_stride = logits_stride;
+    {
+        // the unit counter after the partials and target logits (16-byte aligned)
+        const size_t off = ((size_t)sh.n_parts * n_rows * sizeof(k1::RowPartial) +
+                            (size_t)n_rows * sizeof(float) + 15) & ~(size_t)15;
+        p.done = reinterpret_cast<unsigned*>(reinterpret_cast<char*>(workspace) + off);
+        cudaError_t e = cudaMemsetAsync(p.done, 0, sizeof(unsigned), s);
+        if (e != cudaSuccess) return fail(K1_ERR_CUDA, "%s: %s", fn, cudaGetErrorString(e));
+    }
+    rc = logits_out ? lmh_launch<k1::lmh::STORE>(fn, hidden, weight, n_rows, hidden_dim, vocab,
+                                                 scale, p, sh, s)
+                    : lmh_launch<k1::lmh::STATS>(fn, hidden, weight, n_rows, hidden_dim, vocab,
+                                                 scale, p, sh, s);
+    if (rc) return rc;
+    const int threads = 256;
+    const unsigned blocks = (unsigned)((n_rows + threads - 1) / threads);
+    const unsigned expected =
+        (unsigned)(sh.m_blocks * sh.n_parts) * k1::lmh::EPI_WARPS * (sh.pair ? 2u : 1u);
+    if (partials)
+        k1::lmh::k1_lmhead_shard_merge_kernel<<<blocks, threads, 0, s>>>(
+            p.part, p.xt, targets, n_rows, vocab, col_offset, sh.n_parts, p.done, expected, partials);
+    else
+        k1::lmh::k1_lmhead_merge_kernel<<<blocks, threads, 0, s>>>(
+            p.part, p.xt, targets, n_rows, vocab, sh.n_parts, p.done, expected, logprob, entropy, lse);
+    return check_launch(fn);
+}
+
+// The LM head's backward to the logits (GRAD mode), for a whole vocabulary or a shard.
+int lmh_backward(const char* fn, const void* hidden, const void* weight, int64_t n_rows,
+                 int64_t hidden_dim, int64_t vocab, int64_t col_offset, float scale,
+                 const int64_t* targets, const float* lse, const float* entropy,
+                 const float* g_logp, const float* g_ent, const float* g_lse, void* d_logits,
+                 int64_t d_stride, void* stream) {
+    int rc = lmh_check(fn, hidden, weight, n_rows, hidden_dim, vocab);
+    if (rc) return rc;
+    if (n_rows == 0) return K1_OK;
+    if (!targets || !lse || !entropy || !d_logits)
+        return fail(K1_ERR_INVALID_ARGUMENT, "%s: NULL targets, lse, entropy or d_logits", fn);
+    if (!(scale > 0.f) || !std::isfinite(scale))
+        return fail(K1_ERR_INVALID_ARGUMENT, "%s: scale must be positive and finite", fn);
+    if (d_stride < vocab) return fail(K1_ERR_INVALID_ARGUMENT, "%s: d_stride must be >= vocab", fn);
+    int dev = 0;
+    rc = current_device(&dev);
+    if (rc) return rc;
+    LmhShape sh;
+    rc = lmh_shape(n_rows, hidden_dim, vocab, dev, &sh);
+    if (rc) return rc;
+    k1::lmh::Params p = {};
+    p.col_offset = col_offset;
+    p.targets = targets;
+    p.lse = lse;
+    p.entropy = entropy;
+    p.g_logp = g_logp;
+    p.g_ent = g_ent;
+    p.g_lse = g_lse;
+    p.out = reinterpret_cast<__nv_bfloat16*>(d_logits);
+    p.out_stride = d_stride;
+    return lmh_launch<k1::lmh::GRAD>(fn, hidden, weight, n_rows, hidden_dim, vocab, scale, p, sh,
+                                     reinterpret_cast<cudaStream_t>(stream));
+}
 }  // namespace
 
 extern "C" {
@@ -1104,86 +1201,43 @@ int k1_lm_head_forward(const void* hidden, const void* weight, int64_t n_rows, i
                        float* entropy, float* lse, void* logits_out, int64_t logits_stride,
                        void* workspace, size_t workspace_bytes, void* stream) {
     static const char* fn = "k1_lm_head_forward";
-    int rc = lmh_check(fn, hidden, weight, n_rows, hidden_dim, vocab);
-    if (rc) return rc;
-    if (n_rows == 0) return K1_OK;
-    if (!targets || !logprob || !entropy || !lse)
+    if (n_rows > 0 && (!logprob || !entropy || !lse))
         return fail(K1_ERR_INVALID_ARGUMENT, "%s: NULL targets or output pointer", fn);
-    if (!(scale > 0.f) || !std::isfinite(scale))
-        return fail(K1_ERR_INVALID_ARGUMENT, "%s: scale must be positive and finite", fn);
-    if (logits_out && logits_stride < vocab)
-        return fail(K1_ERR_INVALID_ARGUMENT, "%s: logits_stride must be >= vocab", fn);
-    int dev = 0;
-    rc = current_device(&dev);
-    if (rc) return rc;
-    LmhShape sh;
-    rc = lmh_shape(n_rows, hidden_dim, vocab, dev, &sh);
-    if (rc) return rc;
-    const size_t need = lmh_workspace_bytes(n_rows, sh);
-    if (!workspace || workspace_bytes < need)
-        return fail(K1_ERR_WORKSPACE, "%s: workspace of %zu bytes required (got %zu)", fn, need,
-                    workspace ? workspace_bytes : (size_t)0);
-    if (reinterpret_cast<uintptr_t>(workspace) % 16 != 0)
-        return fail(K1_ERR_INVALID_ARGUMENT, "%s: workspace must be 16-byte aligned", fn);
-    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-    k1::lmh::Params p = {};
-    p.targets = targets;
-    p.part = reinterpret_cast<k1::RowPartial*>(workspace);
-    p.xt = reinterpret_cast<float*>(reinterpret_cast<char*>(workspace) +
-                                    (size_t)sh.n_parts * n_rows * sizeof(k1::RowPartial));
-    p.out = reinterpret_cast<__nv_bfloat16*>(logits_out);
-    p.out_stride = logits_stride;
-    {
-        // the unit counter after the partials and target logits (16-byte aligned)
-        const size_t off = ((size_t)sh.n_parts * n_rows * sizeof(k1::RowPartial) +
-                            (size_t)n_rows * sizeof(float) + 15) & ~(size_t)15;
-        p.done = reinterpret_cast<unsigned*>(reinterpret_cast<char*>(workspace) + off);
-        cudaError_t e = cudaMemsetAsync(p.done, 0, sizeof(unsigned), s);
-        if (e != cudaSuccess) return fail(K1_ERR_CUDA, "%s: %s", fn, cudaGetErrorString(e));
-    }
-    rc = logits_out ? lmh_launch<k1::lmh::STORE>(fn, hidden, weight, n_rows, hidden_dim, vocab,
-                                                 scale, p, sh, s)
-                    : lmh_launch<k1::lmh::STATS>(fn, hidden, weight, n_rows, hidden_dim, vocab,
-                                                 scale, p, sh, s);
-    if (rc) return rc;
-    const int threads = 256;
-    const unsigned expected =
-        (unsigned)(sh.m_blocks * sh.n_parts) * k1::lmh::EPI_WARPS * (sh.pair ? 2u : 1u);
-    k1::lmh::k1_lmhead_merge_kernel<<<(unsigned)((n_rows + threads - 1) / threads), threads, 0, s>>>(
-        p.part, p.xt, targets, n_rows, vocab, sh.n_parts, p.done, expected, logprob, entropy, lse);
-    return check_launch(fn);
+    return lmh_forward(fn, hidden, weight, n_rows, hidden_dim, vocab, 0, scale, targets, logprob,
+                       entropy, lse, nullptr, logits_out, logits_stride, workspace, workspace_bytes,
+                       stream);
+}
+
+int k1_lm_head_shard_partials(const void* hidden, const void* weight_shard, int64_t n_rows,
+                              int64_t hidden_dim, int64_t shard_vocab, int64_t vocab_offset,
+                              float scale, const int64_t* targets, k1_partial* partials,
+                              void* workspace, size_t workspace_bytes, void* stream) {
+    static const char* fn = "k1_lm_head_shard_partials";
+    if (vocab_offset < 0) return fail(K1_ERR_INVALID_ARGUMENT, "%s: vocab_offset must be >= 0", fn);
+    if (n_rows > 0 && !partials) return fail(K1_ERR_INVALID_ARGUMENT, "%s: NULL partials", fn);
+    return lmh_forward(fn, hidden, weight_shard, n_rows, hidden_dim, shard_vocab, vocab_offset, scale,
+                       targets, nullptr, nullptr, nullptr, partials, nullptr, 0, workspace,
+                       workspace_bytes, stream);
 }
 
 int k1_lm_head_backward(const void* hidden, const void* weight, int64_t n_rows, int64_t hidden_dim,
                         int64_t vocab, float scale, const int64_t* targets, const float* lse,
                         const float* entropy, const float* g_logp, const float* g_ent,
                         const float* g_lse, void* d_logits, int64_t d_stride, void* stream) {
-    static const char* fn = "k1_lm_head_backward";
-    int rc = lmh_check(fn, hidden, weight, n_rows, hidden_dim, vocab);
-    if (rc) return rc;
-    if (n_rows == 0) return K1_OK;
-    if (!targets || !lse || !entropy || !d_logits)
-        return fail(K1_ERR_INVALID_ARGUMENT, "%s: NULL targets, lse, entropy or d_logits", fn);
-    if (!(scale > 0.f) || !std::isfinite(scale))
-        return fail(K1_ERR_INVALID_ARGUMENT, "%s: scale must be positive and finite", fn);
-    if (d_stride < vocab) return fail(K1_ERR_INVALID_ARGUMENT, "%s: d_stride must be >= vocab", fn);
-    int dev = 0;
-    rc = current_device(&dev);
-    if (rc) return rc;
-    LmhShape sh;
-    rc = lmh_shape(n_rows, hidden_dim, vocab, dev, &sh);
-    if (rc) return rc;
-    k1::lmh::Params p = {};
-    p.targets = targets;
-    p.lse = lse;
-    p.entropy = entropy;
-    p.g_logp = g_logp;
-    p.g_ent = g_ent;
-    p.g_lse = g_lse;
-    p.out = reinterpret_cast<__nv_bfloat16*>(d_logits);
-    p.out_stride = d_stride;
-    return lmh_launch<k1::lmh::GRAD>(fn, hidden, weight, n_rows, hidden_dim, vocab, scale, p, sh,
-                                     reinterpret_cast<cudaStream_t>(stream));
+    return lmh_backward("k1_lm_head_backward", hidden, weight, n_rows, hidden_dim, vocab, 0, scale,
+                        targets, lse, entropy, g_logp, g_ent, g_lse, d_logits, d_stride, stream);
+}
+
+int k1_lm_head_shard_backward(const void* hidden, const void* weight_shard, int64_t n_rows,
+                              int64_t hidden_dim, int64_t shard_vocab, int64_t vocab_offset,
+                              float scale, const int64_t* targets, const float* lse,
+                              const float* entropy, const float* g_logp, const float* g_ent,
+                              const float* g_lse, void* d_logits, int64_t d_stride, void* stream) {
+    static const char* fn = "k1_lm_head_shard_backward";
+    if (vocab_offset < 0) return fail(K1_ERR_INVALID_ARGUMENT, "%s: vocab_offset must be >= 0", fn);
+    return lmh_backward(fn, hidden, weight_shard, n_rows, hidden_dim, shard_vocab, vocab_offset,
+                        scale, targets, lse, entropy, g_logp, g_ent, g_lse, d_logits, d_stride,
+                        stream);
 }
 
 #ifdef K1_WAIT_TEST

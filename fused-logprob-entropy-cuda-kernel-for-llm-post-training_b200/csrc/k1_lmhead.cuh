@@ -84,7 +84,8 @@ constexpr uint32_t kIdesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN 
 enum Mode : int { STATS = 0, STORE = 1, GRAD = 2 };
 
 struct Params {
-    int64_t n_rows, vocab;
+    int64_t n_rows, vocab;  // vocab: the columns of this weight (a shard of the vocabulary)
+    int64_t col_offset;     // global id of the weight's first row (vocab-parallel shards; else 0)
     int k_blocks;     // ceil(hidden / K per stage); copies beyond `hidden` read zeros
     int m_blocks;     // ceil(n_rows / BM)
     int n_tiles;      // ceil(vocab / BN)
@@ -622,8 +623,9 @@ __global__ void __launch_bounds__(THREADS, 1)
             const Unit x = unit_of(p, u);
             const int64_t row = (int64_t)x.m_blk * GE::TILE_M + (int64_t)rank * BM + rloc;
             const bool live = row < p.n_rows;
-            const int64_t tg = live ? p.targets[row] : -1;
-            const int64_t tcol = (tg >= 0 && tg < p.vocab) ? tg : -1;
+            const int64_t tg = live ? p.targets[row] : -1;  // a global token id
+            const int64_t tt = tg - p.col_offset;
+            const int64_t tcol = (tg >= 0 && tt >= 0 && tt < p.vocab) ? tt : -1;
             FwdState st;
             st.init();
             float xt = 0.f;
@@ -761,6 +763,41 @@ __global__ void __launch_bounds__(THREADS, 1)
                          "r"(TMEM_COLS)
                          : "memory");
     }
+}
+
+// Vocab-parallel shard: the same merge, written as the row's k1_partial (relative to the
+// shard's maximum; the target logit when the target's column lies in the shard) for the
+// all-gather and k1_vocab_combine.  A launch with a missing unit gives NaN partials.
+__global__ void k1_lmhead_shard_merge_kernel(const RowPartial* part, const float* xt,
+                                             const int64_t* targets, int64_t n_rows,
+                                             int64_t vocab, int64_t col_offset, int n_parts,
+                                             const unsigned* done, unsigned expected,
+                                             k1_partial* out) {
+    const int64_t row = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (row >= n_rows) return;
+    k1_partial o;
+    o.reserved = 0;
+    if (*done != expected) {
+        const float nan = __int_as_float(0x7fc00000);
+        o.z = o.t = (double)nan;
+        o.m = o.x_t = nan;
+        o.has_target = 0;
+        out[row] = o;
+        return;
+    }
+    RowPartial acc;
+    acc.m = -INFINITY;
+    acc.z = acc.t = 0.0;
+    acc.pad = 0.f;
+    for (int i = 0; i < n_parts; ++i) acc = merge_partials(acc, part[(int64_t)i * n_rows + row]);
+    const int64_t tg = targets[row], tt = tg - col_offset;
+    const bool has = tg >= 0 && tt >= 0 && tt < vocab;
+    o.m = acc.m;
+    o.z = acc.m == -INFINITY ? 0.0 : acc.z;
+    o.t = acc.m == -INFINITY ? 0.0 : acc.t;
+    o.x_t = has ? xt[row] : 0.f;
+    o.has_target = has ? 1 : 0;
+    out[row] = o;
 }
 
 // Merge the units' partials of every row (fp64, in part order) and finish the row.

@@ -445,6 +445,50 @@ void lm_head_backward(at::Tensor hidden, at::Tensor weight, at::Tensor targets, 
                                      d_logits.stride(0), at::cuda::getCurrentCUDAStream().stream()));
 }
 
+// The LM head over a vocabulary shard (rows [vocab_offset, vocab_offset + weight.size(0)) of
+// the full weight): per-row k1_partial of the shard, for the all-gather and vocab_combine.
+void lm_head_shard_partials(at::Tensor hidden, at::Tensor weight, at::Tensor targets,
+                            int64_t vocab_offset, at::Tensor partials, double scale) {
+    check_lm_head(hidden, weight, targets);
+    const int64_t N = hidden.size(0), H = hidden.size(1), V = weight.size(0);
+    TORCH_CHECK(partials.is_cuda() && partials.scalar_type() == at::kDouble &&
+                    partials.is_contiguous() && partials.numel() == 4 * N,
+                "partials must be a contiguous CUDA float64 tensor of n_rows x 4");
+    if (N == 0) return;
+    c10::cuda::CUDAGuard guard(hidden.device());
+    const size_t ws_bytes = k1_lm_head_workspace_bytes(N, H, V, hidden.get_device());
+    TORCH_CHECK(ws_bytes > 0, "k1: could not size the LM head workspace: ", k1_last_error());
+    at::Tensor ws = at::empty({(int64_t)ws_bytes}, hidden.options().dtype(at::kByte));
+    check_launch(k1_lm_head_shard_partials(
+        hidden.data_ptr(), weight.data_ptr(), N, H, V, vocab_offset, (float)scale,
+        targets.data_ptr<int64_t>(), reinterpret_cast<k1_partial*>(partials.data_ptr()),
+        ws.data_ptr(), ws_bytes, at::cuda::getCurrentCUDAStream().stream()));
+}
+
+void lm_head_shard_backward(at::Tensor hidden, at::Tensor weight, at::Tensor targets,
+                            int64_t vocab_offset, at::Tensor lse, at::Tensor entropy,
+                            c10::optional<at::Tensor> g_logp, c10::optional<at::Tensor> g_ent,
+                            c10::optional<at::Tensor> g_lse, at::Tensor d_logits, double scale) {
+    check_lm_head(hidden, weight, targets);
+    const int64_t N = hidden.size(0), H = hidden.size(1), V = weight.size(0);
+    TORCH_CHECK(lse.scalar_type() == at::kFloat && entropy.scalar_type() == at::kFloat &&
+                    lse.is_contiguous() && entropy.is_contiguous() && lse.numel() == N &&
+                    entropy.numel() == N,
+                "saved lse / entropy must be contiguous fp32 with one entry per row");
+    TORCH_CHECK(d_logits.scalar_type() == at::kBFloat16 && d_logits.dim() == 2 &&
+                    d_logits.size(0) == N && d_logits.size(1) == V && d_logits.stride(1) == 1,
+                "d_logits must be bf16 [N, V_shard] with unit stride along V");
+    const float* gl = opt_grad(g_logp, N, hidden);
+    const float* ge = opt_grad(g_ent, N, hidden);
+    const float* gs = opt_grad(g_lse, N, hidden);
+    if (N == 0) return;
+    c10::cuda::CUDAGuard guard(hidden.device());
+    check_launch(k1_lm_head_shard_backward(
+        hidden.data_ptr(), weight.data_ptr(), N, H, V, vocab_offset, (float)scale,
+        targets.data_ptr<int64_t>(), lse.data_ptr<float>(), entropy.data_ptr<float>(), gl, ge, gs,
+        d_logits.data_ptr(), d_logits.stride(0), at::cuda::getCurrentCUDAStream().stream()));
+}
+
 }  // namespace
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -483,6 +527,18 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
           pybind11::arg("lse"), pybind11::arg("entropy"), pybind11::arg("g_logp"),
           pybind11::arg("g_ent"), pybind11::arg("g_lse"), pybind11::arg("d_logits"),
           pybind11::arg("scale"));
+    m.def("lm_head_shard_partials", &lm_head_shard_partials,
+          "Vocab-parallel LM head: per-row partial state of this rank's weight shard, from "
+          "the tensor-core kernel's epilogue.",
+          pybind11::arg("hidden"), pybind11::arg("weight"), pybind11::arg("targets"),
+          pybind11::arg("vocab_offset"), pybind11::arg("partials"), pybind11::arg("scale"));
+    m.def("lm_head_shard_backward", &lm_head_shard_backward,
+          "Vocab-parallel LM head: K1's gradient w.r.t. this shard's logits, recomputed on "
+          "the tensor cores, from the combined lse / entropy.",
+          pybind11::arg("hidden"), pybind11::arg("weight"), pybind11::arg("targets"),
+          pybind11::arg("vocab_offset"), pybind11::arg("lse"), pybind11::arg("entropy"),
+          pybind11::arg("g_logp"), pybind11::arg("g_ent"), pybind11::arg("g_lse"),
+          pybind11::arg("d_logits"), pybind11::arg("scale"));
     m.def("abi_version", &k1_abi_version, "C ABI version of the loaded libk1_b200.so.");
     m.def(
         "ring_status",

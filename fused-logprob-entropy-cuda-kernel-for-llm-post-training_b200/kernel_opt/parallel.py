@@ -16,6 +16,13 @@ A single all-gather carries everything: NCCL has no reduction operator for the
 (max, sum-exp, sum-exp*x) triple, so a one-collective all-reduce is not available, and
 the max + sum pair of all-reduces would be two collectives.  The backward is local to
 each shard, with the one-hot term applied only on the rank that owns the target.
+
+Vocab-parallel LM head (`vocab_parallel_fused_linear_logprob_entropy`).  The same split
+one step earlier: rank k holds rows [vocab_offset_k, vocab_offset_k + V_k) of the head's
+weight, and step 1 computes the shard's partials in the epilogue of the tensor-core
+LM-head kernel, so no rank writes logits in the forward.  The backward recomputes the
+shard's logits gradient on the tensor cores; the hidden state's gradient is the sum of
+the shards' parts, one all-reduce.
 """
 from __future__ import annotations
 
@@ -101,3 +108,94 @@ def vocab_parallel_fused_logprob_entropy(logits_shard: torch.Tensor, targets: to
     Every rank of `group` must call this with the same row count.
     """
     return _VocabParallelLogprobEntropy.apply(logits_shard, targets, vocab_offset, group)
+
+
+class _VocabParallelLinearLogprobEntropy(torch.autograd.Function):
+    """The tensor-parallel LM head fused with K1 (bf16): this rank holds rows
+    [vocab_offset, vocab_offset + V_k) of the head's [V, H] weight; `hidden` is the same on
+    every rank.  No rank ever holds an [N, V] or [N, V_k] logits tensor in the forward."""
+
+    @staticmethod
+    def forward(ctx, hidden, weight_shard, targets, vocab_offset, scale, group, chunk_rows):
+        n = hidden.shape[0]
+        partials = torch.empty((n, PARTIAL_WORDS), dtype=torch.float64, device=hidden.device)
+        _C.lm_head_shard_partials(hidden, weight_shard, targets, int(vocab_offset), partials,
+                                  scale)
+        gathered = exchange_partials(partials, group)
+        logprob = torch.empty((n,), dtype=torch.float32, device=hidden.device)
+        entropy = torch.empty_like(logprob)
+        lse = torch.empty_like(logprob)
+        _C.vocab_combine(gathered, gathered.shape[0], logprob, entropy, lse)
+        ctx.save_for_backward(hidden, weight_shard, targets, lse, entropy)
+        ctx.vocab_offset = int(vocab_offset)
+        ctx.scale = scale
+        ctx.group = group
+        ctx.chunk_rows = chunk_rows
+        ctx.set_materialize_grads(False)
+        ctx.mark_non_differentiable(lse)
+        return logprob, entropy, lse
+
+    @staticmethod
+    def backward(ctx, g_logp, g_ent, _g_lse):
+        from .lm_head import _chunks, default_chunk_rows
+
+        hidden, w, targets, lse, entropy = ctx.saved_tensors
+        need_h, need_w = ctx.needs_input_grad[0], ctx.needs_input_grad[1]
+        if (g_logp is None and g_ent is None) or not (need_h or need_w):
+            return None, None, None, None, None, None, None
+        gl = None if g_logp is None else g_logp.to(torch.float32).contiguous()
+        ge = None if g_ent is None else g_ent.to(torch.float32).contiguous()
+        n, vk = hidden.shape[0], w.shape[0]
+        c = min(max(1, n), ctx.chunk_rows or default_chunk_rows(n, vk, w.element_size()))
+        dz = torch.empty((c, vk), dtype=hidden.dtype, device=hidden.device)
+        dh32 = torch.empty(hidden.shape, dtype=torch.float32, device=hidden.device) if need_h else None
+        dw32 = torch.zeros(w.shape, dtype=torch.float32, device=w.device) if need_w else None
+        for a, b in _chunks(n, c):
+            d = dz[: b - a]
+            _C.lm_head_shard_backward(hidden[a:b], w, targets[a:b], ctx.vocab_offset, lse[a:b],
+                                      entropy[a:b], None if gl is None else gl[a:b],
+                                      None if ge is None else ge[a:b], None, d, ctx.scale)
+            if need_h:
+                dh32[a:b] = torch.mm(d, w, out_dtype=torch.float32)
+            if need_w:
+                torch.addmm(dw32, d.t(), hidden[a:b], out_dtype=torch.float32, out=dw32)
+        dh = None
+        if need_h:
+            # this shard's part of dL/dhidden; the sum over the shards is the gradient
+            if ctx.group is not None or (dist.is_available() and dist.is_initialized()):
+                dist.all_reduce(dh32, group=ctx.group)
+            dh = dh32.to(hidden.dtype)
+        dw = dw32.to(w.dtype) if need_w else None
+        return dh, dw, None, None, None, None, None
+
+
+def vocab_parallel_fused_linear_logprob_entropy(hidden: torch.Tensor, weight_shard: torch.Tensor,
+                                                targets: torch.Tensor, vocab_offset: int,
+                                                temperature: float = 1.0, group=None,
+                                                chunk_rows: int | None = None):
+    """The LM head fused with K1, split over the vocabulary (tensor-parallel layout).
+
+    hidden: [..., H] bf16, identical on every rank of `group`; weight_shard: [V_k, H] bf16,
+    rows [vocab_offset, vocab_offset + V_k) of the head's [V, H] weight; targets: [...]
+    int64 global token ids.  Returns the full-vocabulary (logprob, entropy, lse) of
+    softmax((hidden @ W.T) / temperature) on every rank, shaped like `targets`.
+
+    Forward: each rank computes its shard's per-row partial state on the tensor cores (the
+    logits never reach memory), ONE all-gather of the [N, 4] float64 partials, and the
+    combine.  Backward: each rank recomputes its shard's logits gradient row chunk by row
+    chunk (`chunk_rows`, default at most 1 GiB of gradient), forms dL/dweight_shard locally
+    and its part of dL/dhidden, and ONE all-reduce (fp32) sums the parts, so every rank
+    gets the full dL/dhidden.  Every rank must call this with the same shapes and the same
+    requires_grad flags (the collectives pair up across ranks).
+    """
+    from .grpo import temperature_scale
+
+    lead = targets.shape
+    h2 = hidden.reshape(-1, hidden.shape[-1])
+    if not h2.is_contiguous():
+        h2 = h2.contiguous()
+    w = weight_shard if weight_shard.is_contiguous() else weight_shard.contiguous()
+    t1 = targets.reshape(-1).contiguous()
+    lp, ent, lse = _VocabParallelLinearLogprobEntropy.apply(
+        h2, w, t1, int(vocab_offset), temperature_scale(temperature), group, chunk_rows)
+    return lp.view(lead), ent.view(lead), lse.view(lead)

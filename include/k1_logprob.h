@@ -267,6 +267,35 @@ int k1_lm_head_backward(const void* hidden, const void* weight, int64_t n_rows, 
                         const float* entropy, const float* g_logp, const float* g_ent,
                         const float* g_lse, void* d_logits, int64_t d_stride, void* stream);
 
+/*
+ * The LM head split over the vocabulary (tensor-parallel head: this rank holds rows
+ * [vocab_offset, vocab_offset + shard_vocab) of the [V, H] weight, weight_shard pointing at
+ * the first).  No counterpart in the reference (single GPU, LM head unbuilt); the rows'
+ * combine is the vocab-parallel one above.
+ *
+ * Forward, step 1 of 3: each row's k1_partial over this shard's logits, computed in the
+ * tensor-core kernel's epilogue (the logits never reach memory); `targets` hold global
+ * token ids.  Workspace: k1_lm_head_workspace_bytes(n_rows, hidden_dim, shard_vocab, dev).
+ * Steps 2 and 3 are the all-gather of the partials and k1_vocab_combine.
+ */
+int k1_lm_head_shard_partials(const void* hidden, const void* weight_shard, int64_t n_rows,
+                              int64_t hidden_dim, int64_t shard_vocab, int64_t vocab_offset,
+                              float scale, const int64_t* targets, k1_partial* partials,
+                              void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * Backward to this shard's logits: k1_lm_head_backward on the shard, with the global lse /
+ * entropy of the combined forward; the one-hot term only where the target lies in the
+ * shard.  d_logits: n_rows x shard_vocab bf16 (rows d_stride >= shard_vocab elements apart).
+ * The caller forms this shard's dL/dweight = d_logits^T hidden and its part of
+ * dL/dhidden = d_logits weight_shard (summed over the shards).
+ */
+int k1_lm_head_shard_backward(const void* hidden, const void* weight_shard, int64_t n_rows,
+                              int64_t hidden_dim, int64_t shard_vocab, int64_t vocab_offset,
+                              float scale, const int64_t* targets, const float* lse,
+                              const float* entropy, const float* g_logp, const float* g_ent,
+                              const float* g_lse, void* d_logits, int64_t d_stride, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

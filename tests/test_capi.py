@@ -155,3 +155,26 @@ def test_lm_head_entry_points_validate_before_the_device(lib):
     lib.k1_lm_head_workspace_bytes.argtypes = [i64, i64, i64, ctypes.c_int]
     lib.k1_lm_head_workspace_bytes.restype = ctypes.c_size_t
     assert lib.k1_lm_head_workspace_bytes(0, 64, 100, 0) == 0
+
+
+def test_lm_head_shard_entry_points_validate_before_the_device(lib):
+    """The vocab-parallel LM head entry points reject a negative vocabulary offset, a NULL
+    partials buffer and the LM head's own bad arguments before any device call."""
+    i64, p, c_float = ctypes.c_int64, ctypes.c_void_p, ctypes.c_float
+    f = lib.k1_lm_head_shard_partials
+    f.argtypes = [p, p, i64, i64, i64, i64, c_float, p, p, p, ctypes.c_size_t, p]
+    f.restype = ctypes.c_int
+    b = lib.k1_lm_head_shard_backward
+    b.argtypes = [p, p, i64, i64, i64, i64, c_float, p, p, p, p, p, p, p, i64, p]
+    b.restype = ctypes.c_int
+    assert f(4096, 8192, 4, 64, 100, -1, 1.0, 1 << 16, 1 << 17, 1 << 18, 1 << 20,
+             None) == K1_ERR_INVALID and "vocab_offset" in _err(lib)
+    assert f(4096, 8192, 4, 64, 100, 200, 1.0, 1 << 16, None, 1 << 18, 1 << 20,
+             None) == K1_ERR_INVALID and "partials" in _err(lib)
+    assert f(4096, 8192, 4, 60, 100, 200, 1.0, 1 << 16, 1 << 17, 1 << 18, 1 << 20,
+             None) == K1_ERR_INVALID and "multiple of 8" in _err(lib)
+    assert f(4096, 8192, 0, 64, 100, 200, 1.0, 1 << 16, None, None, 0, None) == K1_OK
+    assert b(4096, 8192, 4, 64, 100, -5, 1.0, 1 << 16, 1 << 17, 1 << 17, None, None, None,
+             1 << 18, 100, None) == K1_ERR_INVALID and "vocab_offset" in _err(lib)
+    assert b(4096, 8192, 4, 64, 100, 200, 0.0, 1 << 16, 1 << 17, 1 << 17, None, None, None,
+             1 << 18, 100, None) == K1_ERR_INVALID and "scale" in _err(lib)

@@ -229,3 +229,72 @@ def test_tc_gradients_match_materialised_logits(keep, T):
         scale = float(b.float().abs().max())
         torch.testing.assert_close(a.float(), b.float(), rtol=2e-2, atol=1e-3 * scale)
         assert a.dtype == torch.bfloat16
+
+
+def _shards(V, S):
+    from kernel_opt import parallel
+    return [parallel.vocab_shard(V, S, k) for k in range(S)]
+
+
+@pytest.mark.parametrize("shape,S", [((300, 256, 1000), 3), ((129, 3584, 4099), 2),
+                                     ((257, 200, 2064), 4)])
+@pytest.mark.parametrize("T", [1.0, 0.7])
+def test_tc_vocab_shards_combine_to_the_full_head(shape, S, T):
+    """The head split over the vocabulary: each shard's partials (from the tensor-core
+    kernel's epilogue), combined, give the full head's statistics within the north-star
+    tolerances; each shard's recomputed gradient, from the combined lse / entropy, is the
+    full head's gradient on the shard's columns bit for bit."""
+    h, w, t = _tc_problem(*shape, seed=13)
+    N, V = h.shape[0], w.shape[0]
+    t[2] = V - 1          # the last column, in the last shard
+    t[3] = _shards(V, S)[-1].start  # the first column of the last shard
+    scale = grpo.temperature_scale(T)
+    (lp0, ent0, lse0), z = _tc_forward(h, w, t, scale)
+    parts = []
+    for cols in _shards(V, S):
+        p = torch.empty((N, 4), dtype=torch.float64, device="cuda")
+        _C.lm_head_shard_partials(h, w[cols], t, cols.start, p, scale)
+        parts.append(p)
+    gathered = torch.stack(parts)
+    lp, ent, lse = _outs(N)
+    _C.vocab_combine(gathered, S, lp, ent, lse)
+    torch.testing.assert_close(lse, lse0, rtol=0, atol=1e-5)
+    torch.testing.assert_close(lp, lp0, rtol=0, atol=1e-5)
+    torch.testing.assert_close(ent, ent0, rtol=1e-4, atol=1e-7)
+    assert torch.equal(lp[:2], -lse[:2])
+    rows = torch.linspace(0, N - 1, min(64, N)).round().long().unique().cuda()
+    y = (z[rows].float() * scale).to(torch.bfloat16).cpu() if T != 1.0 else z[rows].cpu()
+    check_forward_outputs((lp[rows], ent[rows], lse[rows]), y, t[rows].cpu(), f"shards {shape}")
+
+    g = torch.Generator(device="cuda").manual_seed(6)
+    gl = torch.randn(N, generator=g, device="cuda") * 1e-3
+    ge = torch.randn(N, generator=g, device="cuda") * 1e-4
+    d_full = torch.empty_like(z)
+    _C.lm_head_backward(h, w, t, lse, ent, gl, ge, None, d_full, scale)
+    for cols in _shards(V, S):
+        d = torch.full((N, cols.stop - cols.start), 7.0, dtype=torch.bfloat16, device="cuda")
+        _C.lm_head_shard_backward(h, w[cols], t, cols.start, lse, ent, gl, ge, None, d, scale)
+        assert torch.equal(d, d_full[:, cols]), f"shard {cols} gradient differs"
+
+
+def test_tc_vocab_parallel_head_in_one_process():
+    """Without a process group the vocab-parallel head over the whole weight (one shard)
+    equals the single-GPU fused head, forward and gradients."""
+    from kernel_opt import parallel
+    N, H, V, c = 300, 256, 5003, 128
+    h, w, t, gl, ge = _problem(N, H, V, torch.bfloat16, seed=4)
+    outs = []
+    for fn in (lambda hx, wx: parallel.vocab_parallel_fused_linear_logprob_entropy(
+                   hx, wx, t, 0, 0.7, chunk_rows=c),
+               lambda hx, wx: lm_head.fused_linear_logprob_entropy(hx, wx, t, 0.7, chunk_rows=c)):
+        hx, wx = h.clone().requires_grad_(True), w.clone().requires_grad_(True)
+        lp, ent, lse = fn(hx, wx)
+        dh, dw = torch.autograd.grad((lp, ent), (hx, wx), (gl, ge))
+        outs.append((lp.detach(), ent.detach(), lse.detach(), dh, dw))
+    (lp, ent, lse, dh, dw), (lp0, ent0, lse0, dh0, dw0) = outs
+    torch.testing.assert_close(lse, lse0, rtol=0, atol=1e-5)
+    torch.testing.assert_close(lp, lp0, rtol=0, atol=1e-5)
+    torch.testing.assert_close(ent, ent0, rtol=1e-4, atol=1e-7)
+    # the same d_logits; dh is rounded once from an fp32 product here, dw identically
+    torch.testing.assert_close(dh.float(), dh0.float(), rtol=1e-2, atol=1e-3 * float(dh0.float().abs().max()))
+    assert torch.equal(dw, dw0)

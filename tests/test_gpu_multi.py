@@ -4,7 +4,10 @@
   (shard partials -> one all-gather -> merge) and backward must equal single-GPU K1 on
   the full logits;
 * row-sharded: each rank runs K1 on its block of rows with no collective; gathering the
-  per-row results afterwards must equal K1 over all rows.
+  per-row results afterwards must equal K1 over all rows;
+* vocab-parallel LM head: each rank holds a row shard of the head's weight; the fused
+  tensor-core head (shard partials -> one all-gather -> merge; backward with one
+  all-reduce of the hidden state's gradient) must equal the single-GPU fused head.
 """
 import os
 import socket
@@ -25,6 +28,13 @@ def _free_port():
     port = s.getsockname()[1]
     s.close()
     return port
+
+
+def _head_problem(N, V, H=256):
+    g = torch.Generator().manual_seed(321)
+    hid = (torch.randn(N, H, generator=g) * 0.5).to(torch.bfloat16)
+    wt = (torch.randn(V, H, generator=g) * (2.5 / H ** 0.5)).to(torch.bfloat16)
+    return hid, wt
 
 
 def _worker(rank, world, port, out_dir):
@@ -67,9 +77,17 @@ def _worker(rank, world, port, out_dir):
             parts = [torch.empty(c, device=dev) for c in counts]
             dist.all_gather(parts, o.contiguous())
             gathered.append(torch.cat(parts))
+        # vocab-parallel LM head (bf16, tensor cores)
+        hid, wt = _head_problem(N, V)
+        hx = hid.to(dev).requires_grad_(True)
+        wx = wt[cols].contiguous().to(dev).requires_grad_(True)
+        hl = parallel.vocab_parallel_fused_linear_logprob_entropy(hx, wx, t.to(dev), cols.start,
+                                                                  0.7, chunk_rows=64)
+        dh, dw = torch.autograd.grad(hl[:2], (hx, wx), (gl.to(dev), ge.to(dev)))
         torch.save({"lp": lp.cpu(), "h": h.cpu(), "l": l.cpu(), "d": d.cpu(),
                     "cols": torch.tensor([cols.start, cols.stop]),
-                    "rows": [a.cpu() for a in gathered]},
+                    "rows": [a.cpu() for a in gathered],
+                    "head": [o.detach().cpu() for o in hl], "dh": dh.cpu(), "dw": dw.cpu()},
                    os.path.join(out_dir, f"rank{rank}.pt"))
     finally:
         dist.destroy_process_group()
@@ -102,3 +120,18 @@ def test_vocab_parallel_and_row_sharded_match_single_gpu(tmp_path):
                                    atol=1e-6 * float(d.float().abs().max()))
         for a, b in zip(res["rows"], (lp, h, l)):
             torch.testing.assert_close(a, b.detach().cpu(), rtol=1e-6, atol=4e-6)
+
+    from kernel_opt import lm_head
+    hid, wt = _head_problem(N, V)
+    hx, wx = hid.cuda().requires_grad_(True), wt.cuda().requires_grad_(True)
+    hl = lm_head.fused_linear_logprob_entropy(hx, wx, t.cuda(), 0.7, chunk_rows=64)
+    dh, dw = torch.autograd.grad(hl[:2], (hx, wx), (gl.cuda(), ge.cuda()))
+    for r in range(world):
+        res = torch.load(tmp_path / f"rank{r}.pt")
+        for a, b, rtol in zip(res["head"], hl, (0.0, 1e-4, 0.0)):
+            torch.testing.assert_close(a, b.detach().cpu(), rtol=rtol, atol=1e-5)
+        torch.testing.assert_close(res["dh"].float(), dh.float().cpu(), rtol=1e-2,
+                                   atol=1e-3 * float(dh.float().abs().max()))
+        c0, c1 = (int(v) for v in res["cols"])
+        torch.testing.assert_close(res["dw"].float(), dw[c0:c1].float().cpu(), rtol=1e-2,
+                                   atol=1e-3 * float(dw.float().abs().max()))
