@@ -1265,6 +1265,36 @@ def lmhead_arm(args, cfg, rank, local_rank, world):
            "materialised_train": peak_extra(materialised_step, True),
            "fused_nograd": peak_extra(fused_step, False),
            "materialised_nograd": peak_extra(materialised_step, False)}
+    tp_ms = None
+    if world > 1:
+        # the same full-size head split over the ranks (tensor parallel): rank k holds rows
+        # vocab_shard(V, world, k) of one shared weight; hidden and targets are the same on
+        # every rank.  Forward: shard partials + one all-gather + combine; backward: shard
+        # gradient recomputed + one fp32 all-reduce of dL/dhidden.  Strong scaling.
+        from kernel_opt import parallel
+        cols = parallel.vocab_shard(V, world, rank)
+        g_tp = torch.Generator(device=device).manual_seed(7)
+        h_tp = (torch.randn(N, H, generator=g_tp, device=device) * 0.5).to(dt)
+        t_tp = torch.randint(0, V, (N,), generator=g_tp, device=device)
+        w_tp = ((torch.randn(V, H, generator=g_tp, device=device) * (2.5 / H ** 0.5)).to(dt)
+                [cols].contiguous())
+        torch.cuda.empty_cache()
+
+        def tp_step(grad):
+            hx = h_tp.detach().requires_grad_(grad)
+            wx = w_tp.detach().requires_grad_(grad)
+            lp, ent, _ = parallel.vocab_parallel_fused_linear_logprob_entropy(
+                hx, wx, t_tp, cols.start, T)
+            if grad:
+                torch.autograd.grad((lp, ent), (hx, wx), (g_lp, g_h))
+
+        dist.barrier(device_ids=[local_rank])
+        tp_ms = torch.tensor([timed(tp_step, True, K)], device=device, dtype=torch.float64)
+        dist.barrier(device_ids=[local_rank])
+        tp_ms = torch.cat([tp_ms, torch.tensor([timed(tp_step, False, K)], device=device,
+                                               dtype=torch.float64)])
+        dist.all_reduce(tp_ms, op=dist.ReduceOp.MAX)
+        del h_tp, w_tp
     tt = torch.tensor([res["fused_keep_train_ms"]], device=device, dtype=torch.float64)
     if world > 1:
         dist.all_reduce(tt, op=dist.ReduceOp.MAX)
@@ -1307,6 +1337,21 @@ def lmhead_arm(args, cfg, rank, local_rank, world):
         "gpu_launches": 2 * K,
         "clocks": clocks.summary(),
     }
+    if tp_ms is not None:
+        tr, tn = float(tp_ms[0]), float(tp_ms[1])
+        out["vocab_parallel"] = {
+            "workload": f"the same head split over {world} GPUs: {V} vocabulary rows of W, "
+                        f"{V // world}-{-(-V // world)} per GPU; hidden and targets on every GPU",
+            "scaling": "strong",
+            "train_ms": round(tr, 3), "nograd_ms": round(tn, 3),
+            "train_useful_tflops_total": round(useful / (tr / 1e3) / 1e12, 1),
+            "speedup_train_vs_one_gpu_fused": round(res["fused_train_ms"] / tr, 3),
+            "speedup_nograd_vs_one_gpu_fused": round(res["fused_nograd_ms"] / tn, 3),
+            "collectives": "forward: one NCCL all-gather of [N, 4] float64 partials; backward: "
+                           "one NCCL all-reduce of dL/dhidden [N, H] fp32",
+            "note": "max over ranks of CUDA-event step times; one-GPU figures are this run's "
+                    "fused (memory-light) arms",
+        }
     if sus:
         out["sustained"] = dict(sus, note=f"each kernel back to back for ~{args.lmh_sustained:g} s "
                                           "(at the power cap), the two interleaved, 2 rounds")
