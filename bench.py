@@ -20,6 +20,9 @@ Also on the line:
   vocab_parallel -- config 5 [32768, 256000] over the same N ranks, vocabulary sharded,
       one NCCL all-gather of partials per forward (strong scaling), the all-gather timed
       alone, and a 128-row parity check against an fp64 torch recomputation;
+  lmhead_vocab_parallel -- the LM head [3584 -> 151936] fused with K1 on 16 384 rows, its
+      weight split over the same N ranks (tensor-parallel head, strong scaling): training
+      step and no-grad forward;
   e2e -- the step from pinned host buffers through kernel_opt.host (host<->device copies
       inside the timed region);
   cpu_baseline (N = 1) -- the reference's CPU path on the host cores.
@@ -29,7 +32,7 @@ Metric: algorithmic bytes per step / time, fwd = N V s + 20 N, bwd = 2 N V s + 2
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
                   [--config c2|c3|c4-bf16|c4-fp16|c4-fp32] [--no-cpu-baseline] [--eager]
-                  [--no-extra-configs] [--no-vocab-parallel]
+                  [--no-extra-configs] [--no-vocab-parallel] [--no-lmhead-tp]
                   [--mode rows|vocab|grpo|lmhead]
 
 --impl reference times the reference's CPU path (TRL-1.4 selective_log_softmax +
@@ -610,6 +613,61 @@ def extra_config_legs(device, stream, timer, peak, K, names=("c3", "c4-bf16", "c
     return out
 
 
+def lmhead_tp_leg(args, rank, world, device, stream, barrier, max_over_ranks):
+    """The LM head fused with K1, split over the vocabulary across the ranks (tensor-parallel
+    head), strong scaling: hidden [16384, 3584] bf16 and the targets on every rank, rank k
+    holding rows vocab_shard(151936, world, k) of one [151936, 3584] weight, T = 0.7.
+    Forward = the tensor-core kernel's shard partials + ONE NCCL all-gather + combine;
+    backward = the shard's gradient recomputed on the tensor cores + library GEMMs + ONE
+    NCCL all-reduce of dL/dhidden.  At one GPU: the same call over the whole weight."""
+    from kernel_opt import parallel
+    N, H, V, T = 16384, 3584, 151936, 0.7
+    cols = parallel.vocab_shard(V, world, rank)
+    gen = torch.Generator(device=device).manual_seed(7)
+    h = (torch.randn(N, H, generator=gen, device=device) * 0.5).to(torch.bfloat16)
+    t = torch.randint(0, V, (N,), generator=gen, device=device)
+    w = (torch.randn(V, H, generator=gen, device=device) * (2.5 / H ** 0.5)).to(torch.bfloat16)
+    w = w[cols].contiguous()
+    torch.cuda.empty_cache()
+    g_lp = torch.full((N,), -1.0 / N, device=device)
+    g_h = torch.full((N,), -0.01 / N, device=device)
+
+    def step(grad):
+        hx = h.detach().requires_grad_(grad)
+        wx = w.detach().requires_grad_(grad)
+        with torch.set_grad_enabled(grad):
+            lp, ent, _ = parallel.vocab_parallel_fused_linear_logprob_entropy(hx, wx, t, cols.start, T)
+            if grad:
+                torch.autograd.grad((lp, ent), (hx, wx), (g_lp, g_h))
+
+    K = max(1, min(args.steps, 5))
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    got = {}
+    for name, grad in (("train_ms", True), ("nograd_ms", False)):
+        for _ in range(2):
+            step(grad)
+        barrier()
+        a.record(stream)
+        for _ in range(K):
+            step(grad)
+        b.record(stream)
+        barrier()
+        got[name] = max_over_ranks(a.elapsed_time(b)) / K
+    del h, w
+    torch.cuda.empty_cache()
+    useful = 3 * 2.0 * N * H * V  # forward logits, dL/dhidden, dL/dweight
+    return {"workload": f"LM head [{H} -> {V}] fused with K1 on {N} rows, vocabulary split "
+                        f"over the GPUs ({cols.stop - cols.start} rows of W on rank {rank})",
+            "n_gpus": world, "scaling": "strong", "steps": K, "dtype": "bf16", "temperature": T,
+            "train_ms": round(got["train_ms"], 3), "nograd_ms": round(got["nograd_ms"], 3),
+            "train_useful_tflops_total": round(useful / (got["train_ms"] / 1e3) / 1e12, 1),
+            "collectives": ("forward: one NCCL all-gather of [N, 4] float64 partials; backward: "
+                            "one NCCL all-reduce of dL/dhidden [N, H] fp32" if world > 1
+                            else "none (one process holds the whole weight)"),
+            "note": "max over ranks of CUDA-event time; parity: tests/test_gpu_multi.py, "
+                    "tests/test_gpu_lm_head.py"}
+
+
 def vocab_parallel_leg(args, rank, world, device, stream, barrier, max_over_ranks, peak):
     """Config 5, vocab-parallel (tensor-parallel LM head layout), strong scaling: rank k holds
     columns vocab_shard(256000, world, k) of all 32 768 rows; forward = shard partials, ONE
@@ -875,6 +933,11 @@ def ours_arm(args, cfg, rank, local_rank, world):
         vocab = vocab_parallel_leg(args, rank, world, device, stream, barrier, max_over_ranks,
                                    peak)
 
+    # ---- the tensor-parallel LM head fused with K1 over the same ranks -----------------
+    lmh_tp = None
+    if not args.no_lmhead_tp:
+        lmh_tp = lmhead_tp_leg(args, rank, world, device, stream, barrier, max_over_ranks)
+
     if world > 1:
         dist.barrier(device_ids=[local_rank])
         dist.destroy_process_group()
@@ -935,6 +998,8 @@ def ours_arm(args, cfg, rank, local_rank, world):
         out.update(extra)
     if vocab is not None:
         out["vocab_parallel"] = vocab
+    if lmh_tp is not None:
+        out["lmhead_vocab_parallel"] = lmh_tp
     if cpu is not None:
         out["cpu_baseline"] = cpu
     print(json.dumps(out), flush=True)
@@ -1445,6 +1510,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-extra-configs", action="store_true",
                     help="skip the config 3 / config 4 kernel legs of the N = 1 line")
+    ap.add_argument("--no-lmhead-tp", action="store_true",
+                    help="skip the tensor-parallel LM head record (lmhead_vocab_parallel)")
     ap.add_argument("--no-vocab-parallel", action="store_true",
                     help="skip the config 5 vocab-parallel sub-record")
     ap.add_argument("--lmh-rows", type=int, default=0,
