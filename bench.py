@@ -22,7 +22,7 @@ Also on the line:
       alone, and a 128-row parity check against an fp64 torch recomputation;
   lmhead_vocab_parallel -- the LM head [3584 -> 151936] fused with K1 on 16 384 rows, its
       weight split over the same N ranks (tensor-parallel head, strong scaling): training
-      step and no-grad forward;
+      step (logits recomputed, or kept with keep_logits) and no-grad forward;
   e2e -- the step from pinned host buffers through kernel_opt.host (host<->device copies
       inside the timed region);
   cpu_baseline (N = 1) -- the reference's CPU path on the host cores.
@@ -632,24 +632,26 @@ def lmhead_tp_leg(args, rank, world, device, stream, barrier, max_over_ranks):
     g_lp = torch.full((N,), -1.0 / N, device=device)
     g_h = torch.full((N,), -0.01 / N, device=device)
 
-    def step(grad):
+    def step(grad, keep=False):
         hx = h.detach().requires_grad_(grad)
         wx = w.detach().requires_grad_(grad)
         with torch.set_grad_enabled(grad):
-            lp, ent, _ = parallel.vocab_parallel_fused_linear_logprob_entropy(hx, wx, t, cols.start, T)
+            lp, ent, _ = parallel.vocab_parallel_fused_linear_logprob_entropy(
+                hx, wx, t, cols.start, T, keep_logits=keep)
             if grad:
                 torch.autograd.grad((lp, ent), (hx, wx), (g_lp, g_h))
 
     K = max(1, min(args.steps, 5))
     a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     got = {}
-    for name, grad in (("train_ms", True), ("nograd_ms", False)):
+    for name, grad, keep in (("train_ms", True, False), ("train_keep_ms", True, True),
+                             ("nograd_ms", False, False)):
         for _ in range(2):
-            step(grad)
+            step(grad, keep)
         barrier()
         a.record(stream)
         for _ in range(K):
-            step(grad)
+            step(grad, keep)
         b.record(stream)
         barrier()
         got[name] = max_over_ranks(a.elapsed_time(b)) / K
@@ -660,7 +662,9 @@ def lmhead_tp_leg(args, rank, world, device, stream, barrier, max_over_ranks):
                         f"over the GPUs ({cols.stop - cols.start} rows of W on rank {rank})",
             "n_gpus": world, "scaling": "strong", "steps": K, "dtype": "bf16", "temperature": T,
             "train_ms": round(got["train_ms"], 3), "nograd_ms": round(got["nograd_ms"], 3),
+            "train_keep_ms": round(got["train_keep_ms"], 3),
             "train_useful_tflops_total": round(useful / (got["train_ms"] / 1e3) / 1e12, 1),
+            "train_keep_useful_tflops_total": round(useful / (got["train_keep_ms"] / 1e3) / 1e12, 1),
             "collectives": ("forward: one NCCL all-gather of [N, 4] float64 partials; backward: "
                             "one NCCL all-reduce of dL/dhidden [N, H] fp32" if world > 1
                             else "none (one process holds the whole weight)"),
@@ -1345,19 +1349,22 @@ def lmhead_arm(args, cfg, rank, local_rank, world):
                 [cols].contiguous())
         torch.cuda.empty_cache()
 
-        def tp_step(grad):
+        def tp_step(grad, keep=False):
             hx = h_tp.detach().requires_grad_(grad)
             wx = w_tp.detach().requires_grad_(grad)
             lp, ent, _ = parallel.vocab_parallel_fused_linear_logprob_entropy(
-                hx, wx, t_tp, cols.start, T)
+                hx, wx, t_tp, cols.start, T, keep_logits=keep)
             if grad:
                 torch.autograd.grad((lp, ent), (hx, wx), (g_lp, g_h))
 
-        dist.barrier(device_ids=[local_rank])
-        tp_ms = torch.tensor([timed(tp_step, True, K)], device=device, dtype=torch.float64)
-        dist.barrier(device_ids=[local_rank])
-        tp_ms = torch.cat([tp_ms, torch.tensor([timed(tp_step, False, K)], device=device,
-                                               dtype=torch.float64)])
+        def tp_keep_step(grad):
+            tp_step(grad, keep=True)
+
+        got = []
+        for fn, grad in ((tp_step, True), (tp_step, False), (tp_keep_step, True)):
+            dist.barrier(device_ids=[local_rank])
+            got.append(timed(fn, grad, K))
+        tp_ms = torch.tensor(got, device=device, dtype=torch.float64)
         dist.all_reduce(tp_ms, op=dist.ReduceOp.MAX)
         del h_tp, w_tp
     tt = torch.tensor([res["fused_keep_train_ms"]], device=device, dtype=torch.float64)
@@ -1403,12 +1410,13 @@ def lmhead_arm(args, cfg, rank, local_rank, world):
         "clocks": clocks.summary(),
     }
     if tp_ms is not None:
-        tr, tn = float(tp_ms[0]), float(tp_ms[1])
+        tr, tn, tk = float(tp_ms[0]), float(tp_ms[1]), float(tp_ms[2])
         out["vocab_parallel"] = {
             "workload": f"the same head split over {world} GPUs: {V} vocabulary rows of W, "
                         f"{V // world}-{-(-V // world)} per GPU; hidden and targets on every GPU",
             "scaling": "strong",
-            "train_ms": round(tr, 3), "nograd_ms": round(tn, 3),
+            "train_ms": round(tr, 3), "nograd_ms": round(tn, 3), "train_keep_ms": round(tk, 3),
+            "speedup_train_keep_vs_one_gpu_keep": round(res["fused_keep_train_ms"] / tk, 3),
             "train_useful_tflops_total": round(useful / (tr / 1e3) / 1e12, 1),
             "speedup_train_vs_one_gpu_fused": round(res["fused_train_ms"] / tr, 3),
             "speedup_nograd_vs_one_gpu_fused": round(res["fused_nograd_ms"] / tn, 3),

@@ -1174,6 +1174,22 @@ int k1_vocab_combine(const k1_partial* gathered, int n_shards, int64_t n_rows, f
     return check_launch(fn);
 }
 
+int k1_vocab_shard_scaled_backward(const void* logits, int dtype, int64_t n_rows,
+                                   int64_t shard_vocab, int64_t inner_rows, int64_t inner_stride,
+                                   int64_t outer_stride, int64_t vocab_offset, float scale,
+                                   const int64_t* targets, const float* lse, const float* entropy,
+                                   const float* g_logp, const float* g_ent, const float* g_lse,
+                                   void* d_logits, int64_t d_inner_stride, int64_t d_outer_stride,
+                                   void* stream) {
+    static const char* fn = "k1_vocab_shard_scaled_backward";
+    int rc = check_scale(fn, scale);
+    if (rc) return rc;
+    if (vocab_offset < 0) return fail(K1_ERR_INVALID_ARGUMENT, "%s: vocab_offset must be >= 0", fn);
+    return backward_impl(fn, logits, dtype, n_rows, shard_vocab, inner_rows, inner_stride,
+                         outer_stride, vocab_offset, targets, lse, entropy, g_logp, g_ent, g_lse,
+                         d_logits, d_inner_stride, d_outer_stride, stream, scale);
+}
+
 int k1_vocab_shard_backward(const void* logits, int dtype, int64_t n_rows, int64_t shard_vocab,
                             int64_t inner_rows, int64_t inner_stride, int64_t outer_stride,
                             int64_t vocab_offset, const int64_t* targets, const float* lse,
@@ -1211,13 +1227,14 @@ int k1_lm_head_forward(const void* hidden, const void* weight, int64_t n_rows, i
 int k1_lm_head_shard_partials(const void* hidden, const void* weight_shard, int64_t n_rows,
                               int64_t hidden_dim, int64_t shard_vocab, int64_t vocab_offset,
                               float scale, const int64_t* targets, k1_partial* partials,
-                              void* workspace, size_t workspace_bytes, void* stream) {
+                              void* logits_out, int64_t logits_stride, void* workspace,
+                              size_t workspace_bytes, void* stream) {
     static const char* fn = "k1_lm_head_shard_partials";
     if (vocab_offset < 0) return fail(K1_ERR_INVALID_ARGUMENT, "%s: vocab_offset must be >= 0", fn);
     if (n_rows > 0 && !partials) return fail(K1_ERR_INVALID_ARGUMENT, "%s: NULL partials", fn);
     return lmh_forward(fn, hidden, weight_shard, n_rows, hidden_dim, shard_vocab, vocab_offset, scale,
-                       targets, nullptr, nullptr, nullptr, partials, nullptr, 0, workspace,
-                       workspace_bytes, stream);
+                       targets, nullptr, nullptr, nullptr, partials, logits_out, logits_stride,
+                       workspace, workspace_bytes, stream);
 }
 
 int k1_lm_head_backward(const void* hidden, const void* weight, int64_t n_rows, int64_t hidden_dim,

@@ -277,7 +277,13 @@ void backward_common(const char* which, at::Tensor logits, at::Tensor targets, i
     c10::cuda::CUDAGuard guard(logits.device());
     cudaStream_t s = at::cuda::getCurrentCUDAStream().stream();
     int rc;
-    if (which[0] == 'v') {
+    if (which[0] == 'v' && scale != 1.0) {
+        rc = k1_vocab_shard_scaled_backward(
+            logits.data_ptr(), dt, L.n_rows, L.vocab, L.inner_rows, L.inner_stride, L.outer_stride,
+            vocab_offset, (float)scale, targets.data_ptr<int64_t>(), lse.data_ptr<float>(),
+            entropy.data_ptr<float>(), gl, ge, gs, d_logits.data_ptr(), D.inner_stride,
+            D.outer_stride, s);
+    } else if (which[0] == 'v') {
         rc = k1_vocab_shard_backward(logits.data_ptr(), dt, L.n_rows, L.vocab, L.inner_rows,
                                      L.inner_stride, L.outer_stride, vocab_offset,
                                      targets.data_ptr<int64_t>(), lse.data_ptr<float>(),
@@ -370,9 +376,10 @@ void vocab_combine(at::Tensor gathered, int64_t n_shards, at::Tensor logprob, at
 void vocab_shard_backward(at::Tensor logits, at::Tensor targets, int64_t vocab_offset,
                           at::Tensor lse, at::Tensor entropy, c10::optional<at::Tensor> g_logp,
                           c10::optional<at::Tensor> g_ent, c10::optional<at::Tensor> g_lse,
-                          at::Tensor d_logits) {
+                          at::Tensor d_logits, double scale) {
+    // scale != 1: the shard's logits are read as dtype(x * scale) (temperature folded in)
     backward_common("v", logits, targets, vocab_offset, lse, entropy, g_logp, g_ent, g_lse,
-                    d_logits);
+                    d_logits, scale);
 }
 
 // LM head fused with K1 on the tensor cores (bf16 hidden [N, H] and weight [V, H]).
@@ -448,12 +455,23 @@ void lm_head_backward(at::Tensor hidden, at::Tensor weight, at::Tensor targets, 
 // The LM head over a vocabulary shard (rows [vocab_offset, vocab_offset + weight.size(0)) of
 // the full weight): per-row k1_partial of the shard, for the all-gather and vocab_combine.
 void lm_head_shard_partials(at::Tensor hidden, at::Tensor weight, at::Tensor targets,
-                            int64_t vocab_offset, at::Tensor partials, double scale) {
+                            int64_t vocab_offset, at::Tensor partials, double scale,
+                            c10::optional<at::Tensor> logits_out) {
     check_lm_head(hidden, weight, targets);
     const int64_t N = hidden.size(0), H = hidden.size(1), V = weight.size(0);
     TORCH_CHECK(partials.is_cuda() && partials.scalar_type() == at::kDouble &&
                     partials.is_contiguous() && partials.numel() == 4 * N,
                 "partials must be a contiguous CUDA float64 tensor of n_rows x 4");
+    void* zp = nullptr;
+    int64_t zs = V;
+    if (logits_out.has_value() && logits_out->defined()) {
+        const at::Tensor& z = *logits_out;
+        TORCH_CHECK(z.scalar_type() == at::kBFloat16 && z.dim() == 2 && z.size(0) == N &&
+                        z.size(1) == V && z.stride(1) == 1,
+                    "logits_out must be bf16 [N, V_shard] with unit stride along V");
+        zp = z.data_ptr();
+        zs = z.stride(0);
+    }
     if (N == 0) return;
     c10::cuda::CUDAGuard guard(hidden.device());
     const size_t ws_bytes = k1_lm_head_workspace_bytes(N, H, V, hidden.get_device());
@@ -461,7 +479,7 @@ void lm_head_shard_partials(at::Tensor hidden, at::Tensor weight, at::Tensor tar
     at::Tensor ws = at::empty({(int64_t)ws_bytes}, hidden.options().dtype(at::kByte));
     check_launch(k1_lm_head_shard_partials(
         hidden.data_ptr(), weight.data_ptr(), N, H, V, vocab_offset, (float)scale,
-        targets.data_ptr<int64_t>(), reinterpret_cast<k1_partial*>(partials.data_ptr()),
+        targets.data_ptr<int64_t>(), reinterpret_cast<k1_partial*>(partials.data_ptr()), zp, zs,
         ws.data_ptr(), ws_bytes, at::cuda::getCurrentCUDAStream().stream()));
 }
 
@@ -513,7 +531,12 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
     m.def("vocab_shard_partials", &vocab_shard_partials,
           "Vocab-parallel: per-row partial state of a vocabulary shard.");
     m.def("vocab_combine", &vocab_combine, "Vocab-parallel: merge gathered shard partials.");
-    m.def("vocab_shard_backward", &vocab_shard_backward, "Vocab-parallel: backward of a shard.");
+    m.def("vocab_shard_backward", &vocab_shard_backward,
+          "Vocab-parallel: backward of a shard (scale != 1: logits read as dtype(x * scale)).",
+          pybind11::arg("logits"), pybind11::arg("targets"), pybind11::arg("vocab_offset"),
+          pybind11::arg("lse"), pybind11::arg("entropy"), pybind11::arg("g_logp"),
+          pybind11::arg("g_ent"), pybind11::arg("g_lse"), pybind11::arg("d_logits"),
+          pybind11::arg("scale") = 1.0);
     m.def("lm_head_forward", &lm_head_forward,
           "LM head fused with K1 on the tensor cores: per-row logprob / entropy / lse of "
           "bf16(hidden weight^T) read as bf16(z * scale); optionally also writes z.",
@@ -531,7 +554,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
           "Vocab-parallel LM head: per-row partial state of this rank's weight shard, from "
           "the tensor-core kernel's epilogue.",
           pybind11::arg("hidden"), pybind11::arg("weight"), pybind11::arg("targets"),
-          pybind11::arg("vocab_offset"), pybind11::arg("partials"), pybind11::arg("scale"));
+          pybind11::arg("vocab_offset"), pybind11::arg("partials"), pybind11::arg("scale"),
+          pybind11::arg("logits_out") = pybind11::none());
     m.def("lm_head_shard_backward", &lm_head_shard_backward,
           "Vocab-parallel LM head: K1's gradient w.r.t. this shard's logits, recomputed on "
           "the tensor cores, from the combined lse / entropy.",

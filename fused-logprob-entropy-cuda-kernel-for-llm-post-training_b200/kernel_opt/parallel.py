@@ -116,17 +116,23 @@ class _VocabParallelLinearLogprobEntropy(torch.autograd.Function):
     every rank.  No rank ever holds an [N, V] or [N, V_k] logits tensor in the forward."""
 
     @staticmethod
-    def forward(ctx, hidden, weight_shard, targets, vocab_offset, scale, group, chunk_rows):
+    def forward(ctx, hidden, weight_shard, targets, vocab_offset, scale, group, chunk_rows,
+                keep_logits):
         n = hidden.shape[0]
         partials = torch.empty((n, PARTIAL_WORDS), dtype=torch.float64, device=hidden.device)
+        grad = ctx.needs_input_grad[0] or ctx.needs_input_grad[1]
+        z = torch.empty((n, weight_shard.shape[0]), dtype=hidden.dtype, device=hidden.device) \
+            if (keep_logits and grad) else None
         _C.lm_head_shard_partials(hidden, weight_shard, targets, int(vocab_offset), partials,
-                                  scale)
+                                  scale, z)
         gathered = exchange_partials(partials, group)
         logprob = torch.empty((n,), dtype=torch.float32, device=hidden.device)
         entropy = torch.empty_like(logprob)
         lse = torch.empty_like(logprob)
         _C.vocab_combine(gathered, gathered.shape[0], logprob, entropy, lse)
-        ctx.save_for_backward(hidden, weight_shard, targets, lse, entropy)
+        ctx.save_for_backward(hidden, weight_shard, targets, lse, entropy,
+                              z if z is not None else lse.new_empty(0))
+        ctx.keep = z is not None
         ctx.vocab_offset = int(vocab_offset)
         ctx.scale = scale
         ctx.group = group
@@ -139,12 +145,25 @@ class _VocabParallelLinearLogprobEntropy(torch.autograd.Function):
     def backward(ctx, g_logp, g_ent, _g_lse):
         from .lm_head import _chunks, default_chunk_rows
 
-        hidden, w, targets, lse, entropy = ctx.saved_tensors
+        hidden, w, targets, lse, entropy, z = ctx.saved_tensors
         need_h, need_w = ctx.needs_input_grad[0], ctx.needs_input_grad[1]
         if (g_logp is None and g_ent is None) or not (need_h or need_w):
-            return None, None, None, None, None, None, None
+            return None, None, None, None, None, None, None, None
         gl = None if g_logp is None else g_logp.to(torch.float32).contiguous()
         ge = None if g_ent is None else g_ent.to(torch.float32).contiguous()
+        distributed = ctx.group is not None or (dist.is_available() and dist.is_initialized())
+        if ctx.keep:
+            # K1's backward in place on the kept logits shard, then the library GEMMs
+            _C.vocab_shard_backward(z, targets, ctx.vocab_offset, lse, entropy, gl, ge, None, z,
+                                    ctx.scale)
+            dh = None
+            if need_h:
+                dh32 = torch.mm(z, w, out_dtype=torch.float32)
+                if distributed:
+                    dist.all_reduce(dh32, group=ctx.group)
+                dh = dh32.to(hidden.dtype)
+            dw = torch.mm(z.t(), hidden) if need_w else None
+            return dh, dw, None, None, None, None, None, None
         n, vk = hidden.shape[0], w.shape[0]
         c = min(max(1, n), ctx.chunk_rows or default_chunk_rows(n, vk, w.element_size()))
         dz = torch.empty((c, vk), dtype=hidden.dtype, device=hidden.device)
@@ -162,17 +181,18 @@ class _VocabParallelLinearLogprobEntropy(torch.autograd.Function):
         dh = None
         if need_h:
             # this shard's part of dL/dhidden; the sum over the shards is the gradient
-            if ctx.group is not None or (dist.is_available() and dist.is_initialized()):
+            if distributed:
                 dist.all_reduce(dh32, group=ctx.group)
             dh = dh32.to(hidden.dtype)
         dw = dw32.to(w.dtype) if need_w else None
-        return dh, dw, None, None, None, None, None
+        return dh, dw, None, None, None, None, None, None
 
 
 def vocab_parallel_fused_linear_logprob_entropy(hidden: torch.Tensor, weight_shard: torch.Tensor,
                                                 targets: torch.Tensor, vocab_offset: int,
                                                 temperature: float = 1.0, group=None,
-                                                chunk_rows: int | None = None):
+                                                chunk_rows: int | None = None,
+                                                keep_logits: bool = False):
     """The LM head fused with K1, split over the vocabulary (tensor-parallel layout).
 
     hidden: [..., H] bf16, identical on every rank of `group`; weight_shard: [V_k, H] bf16,
@@ -185,8 +205,11 @@ def vocab_parallel_fused_linear_logprob_entropy(hidden: torch.Tensor, weight_sha
     combine.  Backward: each rank recomputes its shard's logits gradient row chunk by row
     chunk (`chunk_rows`, default at most 1 GiB of gradient), forms dL/dweight_shard locally
     and its part of dL/dhidden, and ONE all-reduce (fp32) sums the parts, so every rank
-    gets the full dL/dhidden.  Every rank must call this with the same shapes and the same
-    requires_grad flags (the collectives pair up across ranks).
+    gets the full dL/dhidden.  `keep_logits=True` trades memory for time as in
+    `fused_linear_logprob_entropy`: the forward also stores this rank's [N, V_k] logits shard
+    and the backward runs K1's backward in place on it instead of recomputing the GEMM.
+    Every rank must call this with the same shapes and the same requires_grad flags (the
+    collectives pair up across ranks).
     """
     from .grpo import temperature_scale
 
@@ -197,5 +220,6 @@ def vocab_parallel_fused_linear_logprob_entropy(hidden: torch.Tensor, weight_sha
     w = weight_shard if weight_shard.is_contiguous() else weight_shard.contiguous()
     t1 = targets.reshape(-1).contiguous()
     lp, ent, lse = _VocabParallelLinearLogprobEntropy.apply(
-        h2, w, t1, int(vocab_offset), temperature_scale(temperature), group, chunk_rows)
+        h2, w, t1, int(vocab_offset), temperature_scale(temperature), group, chunk_rows,
+        bool(keep_logits))
     return lp.view(lead), ent.view(lead), lse.view(lead)

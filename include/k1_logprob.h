@@ -227,6 +227,19 @@ int k1_vocab_shard_backward(
     void* stream);
 
 /*
+ * The same with the temperature folded in (the shard's logits read as dtype(x * scale),
+ * as k1_fused_logprob_entropy_scaled_backward): the backward of a vocab-parallel LM head
+ * that kept its logits shard.  d_logits may alias logits (in place).  No counterpart in
+ * the reference.
+ */
+int k1_vocab_shard_scaled_backward(
+    const void* logits, int dtype, int64_t n_rows, int64_t shard_vocab, int64_t inner_rows,
+    int64_t inner_stride, int64_t outer_stride, int64_t vocab_offset, float scale,
+    const int64_t* targets, const float* lse, const float* entropy, const float* g_logp,
+    const float* g_ent, const float* g_lse, void* d_logits, int64_t d_inner_stride,
+    int64_t d_outer_stride, void* stream);
+
+/*
  * LM head fused with K1 on the tensor cores (tcgen05).  The reference names this as its
  * follow-up and leaves it unbuilt (README.md:135-136, docs/FINAL_REPORT.md:490-494); the
  * unfused sequence it replaces is the model's LM head GEMM, then the trainer's
@@ -274,14 +287,18 @@ int k1_lm_head_backward(const void* hidden, const void* weight, int64_t n_rows, 
  * combine is the vocab-parallel one above.
  *
  * Forward, step 1 of 3: each row's k1_partial over this shard's logits, computed in the
- * tensor-core kernel's epilogue (the logits never reach memory); `targets` hold global
- * token ids.  Workspace: k1_lm_head_workspace_bytes(n_rows, hidden_dim, shard_vocab, dev).
+ * tensor-core kernel's epilogue; `targets` hold global token ids.  logits_out = NULL: the
+ * logits never reach memory; otherwise the shard's z is also written (rows logits_stride
+ * >= shard_vocab elements apart) for a backward that keeps it
+ * (k1_vocab_shard_scaled_backward).  Workspace: k1_lm_head_workspace_bytes(n_rows,
+ * hidden_dim, shard_vocab, dev).
  * Steps 2 and 3 are the all-gather of the partials and k1_vocab_combine.
  */
 int k1_lm_head_shard_partials(const void* hidden, const void* weight_shard, int64_t n_rows,
                               int64_t hidden_dim, int64_t shard_vocab, int64_t vocab_offset,
                               float scale, const int64_t* targets, k1_partial* partials,
-                              void* workspace, size_t workspace_bytes, void* stream);
+                              void* logits_out, int64_t logits_stride, void* workspace,
+                              size_t workspace_bytes, void* stream);
 
 /*
  * Backward to this shard's logits: k1_lm_head_backward on the shard, with the global lse /

@@ -162,18 +162,29 @@ def test_lm_head_shard_entry_points_validate_before_the_device(lib):
     partials buffer and the LM head's own bad arguments before any device call."""
     i64, p, c_float = ctypes.c_int64, ctypes.c_void_p, ctypes.c_float
     f = lib.k1_lm_head_shard_partials
-    f.argtypes = [p, p, i64, i64, i64, i64, c_float, p, p, p, ctypes.c_size_t, p]
+    f.argtypes = [p, p, i64, i64, i64, i64, c_float, p, p, p, i64, p, ctypes.c_size_t, p]
     f.restype = ctypes.c_int
     b = lib.k1_lm_head_shard_backward
     b.argtypes = [p, p, i64, i64, i64, i64, c_float, p, p, p, p, p, p, p, i64, p]
     b.restype = ctypes.c_int
-    assert f(4096, 8192, 4, 64, 100, -1, 1.0, 1 << 16, 1 << 17, 1 << 18, 1 << 20,
+    assert f(4096, 8192, 4, 64, 100, -1, 1.0, 1 << 16, 1 << 17, None, 100, 1 << 18, 1 << 20,
              None) == K1_ERR_INVALID and "vocab_offset" in _err(lib)
-    assert f(4096, 8192, 4, 64, 100, 200, 1.0, 1 << 16, None, 1 << 18, 1 << 20,
+    assert f(4096, 8192, 4, 64, 100, 200, 1.0, 1 << 16, None, None, 100, 1 << 18, 1 << 20,
              None) == K1_ERR_INVALID and "partials" in _err(lib)
-    assert f(4096, 8192, 4, 60, 100, 200, 1.0, 1 << 16, 1 << 17, 1 << 18, 1 << 20,
+    assert f(4096, 8192, 4, 60, 100, 200, 1.0, 1 << 16, 1 << 17, None, 100, 1 << 18, 1 << 20,
              None) == K1_ERR_INVALID and "multiple of 8" in _err(lib)
-    assert f(4096, 8192, 0, 64, 100, 200, 1.0, 1 << 16, None, None, 0, None) == K1_OK
+    assert f(4096, 8192, 4, 64, 100, 200, 1.0, 1 << 16, 1 << 17, 1 << 19, 99, 1 << 18, 1 << 20,
+             None) == K1_ERR_INVALID and "logits_stride" in _err(lib)
+    assert f(4096, 8192, 0, 64, 100, 200, 1.0, 1 << 16, None, None, 0, None, 0, None) == K1_OK
+    sb = lib.k1_vocab_shard_scaled_backward
+    sb.argtypes = [p, ctypes.c_int, i64, i64, i64, i64, i64, i64, c_float, p, p, p, p, p, p, p,
+                   i64, i64, p]
+    sb.restype = ctypes.c_int
+    for s in (0.0, float("nan")):
+        assert sb(1024, 2, 4, 16, 4, 16, 0, 0, s, 2048, 4096, 4096, None, None, None, 8192, 16, 0,
+                  None) == K1_ERR_INVALID and "scale" in _err(lib)
+    assert sb(1024, 2, 4, 16, 4, 16, 0, -3, 1.5, 2048, 4096, 4096, None, None, None, 8192, 16, 0,
+              None) == K1_ERR_INVALID and "vocab_offset" in _err(lib)
     assert b(4096, 8192, 4, 64, 100, -5, 1.0, 1 << 16, 1 << 17, 1 << 17, None, None, None,
              1 << 18, 100, None) == K1_ERR_INVALID and "vocab_offset" in _err(lib)
     assert b(4096, 8192, 4, 64, 100, 200, 0.0, 1 << 16, 1 << 17, 1 << 17, None, None, None,

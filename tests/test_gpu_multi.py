@@ -84,6 +84,15 @@ def _worker(rank, world, port, out_dir):
         hl = parallel.vocab_parallel_fused_linear_logprob_entropy(hx, wx, t.to(dev), cols.start,
                                                                   0.7, chunk_rows=64)
         dh, dw = torch.autograd.grad(hl[:2], (hx, wx), (gl.to(dev), ge.to(dev)))
+        # keep_logits: the same results from the kept logits shard
+        hk = parallel.vocab_parallel_fused_linear_logprob_entropy(hx, wx, t.to(dev), cols.start,
+                                                                  0.7, keep_logits=True)
+        dhk, dwk = torch.autograd.grad(hk[:2], (hx, wx), (gl.to(dev), ge.to(dev)))
+        assert all(torch.equal(a, b) for a, b in zip(hk, hl))
+        torch.testing.assert_close(dhk.float(), dh.float(), rtol=1e-2,
+                                   atol=1e-3 * float(dh.float().abs().max()))
+        torch.testing.assert_close(dwk.float(), dw.float(), rtol=1e-2,
+                                   atol=1e-3 * float(dw.float().abs().max()))
         torch.save({"lp": lp.cpu(), "h": h.cpu(), "l": l.cpu(), "d": d.cpu(),
                     "cols": torch.tensor([cols.start, cols.stop]),
                     "rows": [a.cpu() for a in gathered],
